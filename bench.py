@@ -1,0 +1,391 @@
+"""MoE-layer forward throughput on B200 (tokens/s), one JSON line on rank 0.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config edge|edge_skewed|pro|proxy_tiny]
+                  [--impl ours|reference]
+
+A step is one ParallelFFN forward (router, permute, grouped SwiGLU expert
+GEMMs, dense GeGLU branch, combine) over one batch of seeded synthetic tokens,
+all inputs resident in HBM.  With N > 1 (torchrun, one process per GPU) the
+experts are sharded expert-parallel E/N per rank and every rank routes its own
+batch: the Edge-like layer keeps 16384 tokens per rank (weak scaling), the
+Pro-like layer splits its 131072 tokens across ranks (strong scaling).
+
+`--impl reference` times the reference's CPU algorithm for the same layer (the
+oracle port of crates/noor-core MoELayer/ParallelFFN, per-token m=1 OpenBLAS
+sgemm as the reference's cblas route) on this host's cores, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+pkg = importlib.import_module("noor_-_bangla_ai_b200")
+W = pkg.workloads
+
+METRIC = "MoE-layer tokens/sec"
+UNIT = "tokens/s"
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_FLUSH_BYTES = 256 << 20
+
+
+def peaks():
+    try:
+        with open(PEAKS_PATH) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return FALLBACK_PEAKS, "fallback"
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def layer_tokens(cfg, world):
+    """Tokens per rank and the scaling mode."""
+    if cfg.name == "pro":
+        return cfg.tokens // world, "strong"
+    return cfg.tokens, "weak"
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU baseline
+
+def cpu_baseline(cfg, w, x_sample, steps: int = 1):
+    """The oracle port of the reference path on this host's cores, OpenBLAS
+    threads = all cores; returns (tokens/s, cores, seconds)."""
+    from oracle import oracle as O
+    cores = os.cpu_count() or 1
+    blas = O.use_openblas(cores)
+    try:
+        O.parallel_forward(w, x_sample[:8], cfg.top_k)  # warm the BLAS
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            O.parallel_forward(w, x_sample, cfg.top_k)
+        dt = time.perf_counter() - t0
+    finally:
+        O.use_plain_loops()
+    return x_sample.shape[0] * steps / dt, (cores if blas else 1), dt, blas
+
+
+def cpu_sample_tokens(cfg):
+    return {"proxy_tiny": 2048, "edge": 512, "edge_skewed": 512, "pro": 256}.get(cfg.name, 512)
+
+
+# ------------------------------------------------------------------ reference arm
+
+def run_reference(args):
+    rank, _, world = env_rank()
+    if rank != 0:
+        return 0
+    cfg = W.CONFIGS[args.config]
+    T_rank, scaling = layer_tokens(cfg, world)
+    w = W.make_weights(cfg)
+    n = cpu_sample_tokens(cfg)
+    x = W.make_tokens(cfg, tokens=n)
+    from oracle import oracle as O
+    cores = os.cpu_count() or 1
+    blas = O.use_openblas(cores)
+    times = []
+    try:
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            O.parallel_forward(w, x, cfg.top_k)
+            dt = time.perf_counter() - t0
+            if i >= args.warmup:
+                times.append(dt)
+    finally:
+        O.use_plain_loops()
+    tot = sum(times)
+    value = n * len(times) / tot
+    sample = (f"{n} tokens of the {cfg.name} layer per step (contiguous from the seeded batch); "
+              f"per-token MoE loop with m=1 OpenBLAS sgemm + batched dense GeGLU, as the reference's "
+              f"cblas route; {'OpenBLAS' if blas else 'plain loops'}")
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot / len(times),
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Philox, reference layouts)",
+        "config": config_dict(cfg, T_rank, world, scaling),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores if blas else 1, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_dict(cfg, T_rank, world, scaling):
+    return {"workload": f"{cfg.name} MoE layer (ParallelFFN forward)", "tokens_per_rank": T_rank,
+            "global_tokens": T_rank * world, "d_model": cfg.d_model, "n_experts": cfg.n_experts,
+            "top_k": cfg.top_k, "expert_ff": cfg.expert_ff, "dense_ff": cfg.dense_ff,
+            "dense_act": "gelu_tanh (GeGLU)", "parallelism": f"ep{world}" if world > 1 else "single",
+            "experts_per_rank": cfg.n_experts // world, "l2": "flushed (256 MiB write between steps, "
+            "outside the timed events)", "scaling": scaling}
+
+
+# ------------------------------------------------------------------ our arm
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    rank, local_rank, world = env_rank()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=300))
+    cfg = W.CONFIGS[args.config]
+    T, scaling = layer_tokens(cfg, world)
+    w = W.make_weights(cfg)
+    x = W.make_tokens(cfg, seed_offset=1 + 7919 * rank, tokens=T)
+    xb = W.bf16_bits(x) if cfg.dtype == W.BF16 else x
+
+    comm = None
+    if world > 1:
+        uid = pkg.api.comm_get_id() if rank == 0 else bytes(pkg.api.lib().noor_moe_comm_id_size())
+        t = torch.tensor(list(uid), dtype=torch.uint8, device=dev)
+        dist.broadcast(t, 0)
+        comm = pkg.api.comm_init_rank(bytes(t.cpu().tolist()), world, rank, local_rank)
+    h = pkg.api.Handle(cfg.d_model, cfg.n_experts, cfg.top_k, cfg.expert_ff, cfg.dense_ff, dtype=cfg.dtype,
+                       device=local_rank, world_size=world, rank=rank, max_tokens=T, comm=comm)
+    h.load_weights(w)
+
+    tdt = torch.int16 if cfg.dtype == W.BF16 else torch.float32
+    x_host = torch.from_numpy(xb.view(np.int16) if cfg.dtype == W.BF16 else xb).pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    x_dev = x_host.to(dev)
+    out_dev = torch.empty_like(x_dev)
+    counts = torch.empty(cfg.n_experts, dtype=torch.int64, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sid = stream.cuda_stream
+
+    def step():
+        h.forward_device(x_dev.data_ptr(), out_dev.data_ptr(), T, sid, counts_ptr=counts.data_ptr())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    barrier()
+
+    # ---- timed region: device events around each step, L2 flushed in between
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    launches0 = h.launch_count()
+    h.profile_begin(args.steps * 32)
+    barrier()
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    barrier()
+    prof = h.profile_end()
+    launches = h.launch_count() - launches0
+    clocks = sampler.stop()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    tot_ms = sum(step_ms)
+    if world > 1:
+        tt = torch.tensor([tot_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        tot_ms = float(tt.item())
+        lt = torch.tensor([launches], dtype=torch.int64, device=dev)
+        dist.all_reduce(lt)
+        launches = int(lt.item())
+    value = T * world * args.steps / (tot_ms / 1e3)
+
+    # ---- end to end through the public API: pinned host in, pinned host out
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(2):
+        x_dev.copy_(x_host, non_blocking=True)
+        step()
+        out_host.copy_(out_dev, non_blocking=True)
+    barrier()
+    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_steps)]
+    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_steps)]
+    for i in range(e2e_steps):
+        flush.zero_()
+        e_s[i].record(stream)
+        x_dev.copy_(x_host, non_blocking=True)
+        step()
+        out_host.copy_(out_dev, non_blocking=True)
+        e_e[i].record(stream)
+    barrier()
+    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_s, e_e))
+    if world > 1:
+        tt = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    e2e = T * world * e2e_steps / (e2e_ms / 1e3)
+    io_bytes = int(x_host.numel() * x_host.element_size())
+
+    # ---- roofline of each kernel from the live per-launch events
+    pk, pk_kind = peaks()
+    rows_local = int(counts.sum().item()) if world == 1 else None
+    kern = kernel_rooflines(cfg, T, world, prof, pk, pk_kind, h, counts)
+
+    line = None
+    if rank == 0:
+        dom = kern.get("expert_gemm1")
+        roof = None
+        if dom:
+            roof = {"bound": "tensor", "kernel": "expert_gemm1 (grouped SwiGLU gate/up, tcgen05)",
+                    "achieved": dom["achieved"], "peak": dom["peak"], "unit": "TFLOP/s",
+                    "frac": dom["frac"], "traffic": None,
+                    "peak_source": f"bf16_tflops_sustained, {pk_kind}",
+                    "algorithmic_per_launch": dom["algorithmic_per_launch"],
+                    "avg_launch_ms": dom["avg_ms"]}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": tot_ms / args.steps, "higher_is_better": True,
+            "scaling": scaling, "vs_baseline": None, "dtype": "bf16" if cfg.dtype == W.BF16 else "f32",
+            "data": "synthetic (seeded Philox; x = RMSNorm(N(0,1)), weights N(0,0.02), bias U(-0.1,0.1))",
+            "config": config_dict(cfg, T, world, scaling),
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes,
+                    "api": "noor_moe_forward (device mode) with pinned-host H2D/D2H in the timed region"},
+            "gpu_launches": launches,
+            "roofline": roof,
+            "kernels": kern,
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            n = cpu_sample_tokens(cfg)
+            xs = np.ascontiguousarray(x[:n])
+            v, cores, dt, blas = cpu_baseline(cfg, w, xs)
+            line["cpu_baseline"] = {
+                "value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                "sample": f"{n} contiguous tokens of this batch through the oracle port of the reference "
+                          f"ParallelFFN/MoELayer forward ({'OpenBLAS sgemm' if blas else 'plain loops'}), "
+                          f"{dt:.1f} s"}
+    h.close()
+    if comm:
+        pkg.api.comm_destroy(comm)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def kernel_rooflines(cfg, T, world, prof, pk, pk_kind, h, counts):
+    """Per-kernel achieved rate from the live events: algorithmic FLOPs or
+    bytes per launch / average launch time."""
+    d, E, k, ff, dff = cfg.d_model, cfg.n_experts, cfg.top_k, cfg.expert_ff, cfg.dense_ff
+    b = 2 if cfg.dtype == W.BF16 else 4
+    R = T * k  # picks routed per rank (rows an expert GEMM processes per rank under uniform routing)
+    tf = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+    hbm = pk.get("hbm_gbs")
+    by = W.algorithmic_bytes(cfg, T)
+    spec = {
+        "router": ("hbm", by["router"]),
+        "permute": ("hbm", by["permute"]),
+        "combine": ("hbm", by["combine"]),
+        "expert_gemm1": ("tensor", 2.0 * R * d * 2 * ff),
+        "expert_gemm2": ("tensor", 2.0 * R * ff * d),
+        "dense_gemm1": ("tensor", 2.0 * T * d * 2 * dff),
+        "dense_gemm2": ("tensor", 2.0 * T * dff * d),
+    }
+    out = {}
+    for name, v in prof.items():
+        avg = v["total_ms"] / max(1, v["launches"])
+        ent = {"avg_ms": avg, "launches": v["launches"]}
+        if name in spec and cfg.dtype == W.BF16:
+            bound, amount = spec[name]
+            if bound == "tensor":
+                ach = amount / (avg / 1e3) / 1e12
+                ent.update(bound="tensor", achieved=ach, unit="TFLOP/s", peak=tf, frac=ach / tf,
+                           algorithmic_per_launch=amount)
+            else:
+                ach = amount / (avg / 1e3) / 1e9
+                ent.update(bound="hbm", achieved=ach, unit="GB/s", peak=hbm, frac=ach / hbm,
+                           algorithmic_per_launch=amount)
+        out[name] = ent
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="edge", choices=sorted(W.CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,176 @@
+/*
+ * noor_moe.h -- C ABI of the B200 (sm_100a) sparse-MoE layer forward.
+ *
+ * This is the drop-in boundary for Noor's noor-core MoE path.  Today the Rust
+ * layer code calls a matmul-level FFI (crates/noor-core/src/kernels.rs:141,
+ * `matmul_dispatch`, which reaches cblas_sgemm / noor_matmul_f32 / cuBLAS,
+ * kernels.rs:6-51, 93-137).  The entry points below replace it at layer level
+ * so that `MoELayer::forward` (crates/noor-core/src/layers/moe.rs:145) and
+ * `ParallelFFN::forward` (crates/noor-core/src/layers/parallel_ffn.rs:30) keep
+ * their signatures and hand the whole layer to the GPU in one call.
+ *
+ * Conventions (all entry points):
+ *  - every function returns an int status, NOOR_MOE_OK (0) on success; the
+ *    library never aborts the process.  noor_moe_last_error() gives a
+ *    thread-local message for the last failure on the calling thread;
+ *  - the caller owns input and output buffers; the library owns device
+ *    weights and workspaces;
+ *  - pointer mode is chosen by `stream`: stream == NULL means host pointers
+ *    and a synchronous call (the reference returns Tensors by value);
+ *    stream != NULL means device pointers, enqueued on that cudaStream_t;
+ *  - a handle is bound to one (layer, device) and is not re-entrant; distinct
+ *    handles may be used from distinct threads.
+ */
+#ifndef NOOR_MOE_H
+#define NOOR_MOE_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NOOR_MOE_API __attribute__((visibility("default")))
+#else
+#define NOOR_MOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NOOR_MOE_OK 0
+#define NOOR_MOE_ERR_INVALID 1     /* bad argument or shape */
+#define NOOR_MOE_ERR_CUDA 2        /* a CUDA runtime/driver call failed */
+#define NOOR_MOE_ERR_NCCL 3        /* an NCCL call failed or timed out */
+#define NOOR_MOE_ERR_OOM 4         /* device allocation failed */
+#define NOOR_MOE_ERR_STATE 5       /* call out of order (e.g. forward before weights) */
+#define NOOR_MOE_ERR_TIMEOUT 6     /* a device-side bounded wait gave up */
+#define NOOR_MOE_ERR_UNSUPPORTED 7 /* shape outside what the kernels implement */
+
+#define NOOR_DTYPE_F32 0   /* f32 storage and f32 CUDA-core math (the reference's dtype) */
+#define NOOR_DTYPE_BF16 1  /* BF16 storage, tcgen05 tensor cores, f32 accumulation */
+
+#define NOOR_ACT_GELU_TANH 0 /* GeGLU dense branch, tensor.rs:438-449 (reference default) */
+#define NOOR_ACT_SILU 1      /* SwiGLU */
+
+/* Layer descriptor.  Mirrors the `[moe]` config block
+ * (crates/noor-core/src/config.rs:32-39) and ParallelFFN::new
+ * (parallel_ffn.rs:14-27). */
+typedef struct {
+  int32_t d_model;
+  int32_t n_experts;   /* E */
+  int32_t top_k;       /* n_active; clamped to E like moe.rs:99 */
+  int32_t expert_ff;   /* SwiGLU expert hidden size */
+  int32_t dense_ff;    /* parallel dense branch hidden size */
+  int32_t has_shared;  /* unweighted shared SwiGLU expert (moe.rs:168-173) */
+  int32_t has_dense;   /* 1: ParallelFFN::forward, (dense + moe)/sqrt(2); 0: MoELayer::forward */
+  int32_t dtype;       /* NOOR_DTYPE_* */
+  int32_t dense_act;   /* NOOR_ACT_*; the reference's dense branch is GELU_TANH */
+  int32_t device;      /* CUDA ordinal this handle lives on */
+  int32_t world_size;  /* expert-parallel group size (1 = single GPU) */
+  int32_t rank;        /* this process's rank in the group */
+  int64_t max_tokens;  /* tokens per call the workspaces are sized for (grown on demand) */
+} noor_moe_desc;
+
+typedef struct noor_moe_handle noor_moe_handle;
+
+/* Create a layer handle.  `nccl_comm` is an ncclComm_t spanning world_size
+ * ranks (from noor_moe_comm_init_rank), or NULL when world_size == 1.
+ * Replaces constructing MoELayer / ParallelFFN (moe.rs:119-143,
+ * parallel_ffn.rs:14-27) on the host. */
+NOOR_MOE_API int noor_moe_create(const noor_moe_desc* desc, void* nccl_comm, noor_moe_handle** out);
+
+/* Upload weights given in the reference's f32 row-major layouts; the library
+ * rounds to BF16 (RNE, tensor.rs:23-28) for BF16 layers and prepacks them
+ * K-major for the tensor cores.  Expert arrays hold E pointers (one Tensor per
+ * SwiGLUFFN in Vec<SwiGLUFFN>, moe.rs:112); under expert parallelism only the
+ * rank's own E/world_size entries are read and the rest may be NULL.
+ *   gate   [d, E]   MoERouter::gate (moe.rs:7)
+ *   bias   [E]      MoERouter::expert_biases (SMEBU, moe.rs:9)
+ *   scales [E]      MoERouter::expert_scales (moe.rs:11)
+ *   w_gate[e], w_up[e] [d, ff];  w_down[e] [ff, d]   (ffn.rs:43-50)
+ *   shared[3]  nullable {w_gate, w_up, w_down} of the shared expert
+ *   dense[3]   {w_gate [d,dff], w_up [d,dff], w_down [dff,d]} (ffn.rs:5-12); NULL if has_dense == 0 */
+NOOR_MOE_API int noor_moe_load_weights(noor_moe_handle* h, const float* gate, const float* bias,
+                          const float* scales, const float* const* w_gate,
+                          const float* const* w_up, const float* const* w_down,
+                          const float* const* shared, const float* const* dense);
+
+/* Replace the SMEBU router bias (host f32 [E]); the per-step path of
+ * SMEBU::apply_to_router (crates/noor-train/src/optim/smebu.rs:56-61). */
+NOOR_MOE_API int noor_moe_set_bias(noor_moe_handle* h, const float* bias);
+
+/* Layer forward over T tokens: MoELayer::forward (moe.rs:145-177) when
+ * has_dense == 0, ParallelFFN::forward (parallel_ffn.rs:30-36) otherwise.
+ * x [T, d] and out [T, d] are f32 for F32 layers and BF16 bit patterns
+ * (uint16) for BF16 layers.  Optional outputs (NULL to skip):
+ *   topk_idx [T, k] int32   RouteResult::indices, rank order (moe.rs:17-22)
+ *   topk_w   [T, k] f32     RouteResult::weights = sigmoid score * scale
+ *   expert_counts [E] int64 this call's ExpertUtilization::record counts
+ *                           (moe.rs:40-45), summed over all ranks under EP
+ * In device mode (stream != NULL) all pointers are device pointers.
+ * Under expert parallelism every rank calls this collectively with its own
+ * T tokens. */
+NOOR_MOE_API int noor_moe_forward(noor_moe_handle* h, const void* x, void* out, int64_t T, int32_t* topk_idx,
+                     float* topk_w, int64_t* expert_counts, void* stream);
+
+/* Router only: the batched form of MoERouter::route (moe.rs:79-107) plus the
+ * utilization histogram.  Same pointer and dtype rules as noor_moe_forward;
+ * idx and w are required, counts may be NULL. */
+NOOR_MOE_API int noor_moe_route(noor_moe_handle* h, const void* x, int64_t T, int32_t* idx, float* w,
+                   int64_t* counts, void* stream);
+
+/* Matmul-level entry point, the live route of kernels.rs:141-163
+ * (cblas_sgemm row-major, alpha = 1, beta = 0): C[m,n] = A[m,k] . B[k,n],
+ * f32, host pointers, C overwritten.  Runs on the current device. */
+NOOR_MOE_API int noor_matmul_f32(const float* a, const float* b, float* c, int64_t m, int64_t k, int64_t n);
+
+/* Thread-local message describing the last failure on this thread ("" if none). */
+NOOR_MOE_API const char* noor_moe_last_error(void);
+
+/* Wait for the handle's work on `stream` (NULL = its internal stream) and
+ * report any error a kernel flagged on the device (e.g. a bounded wait that
+ * timed out, NOOR_MOE_ERR_TIMEOUT).  Clears the flag. */
+NOOR_MOE_API int noor_moe_sync(noor_moe_handle* h, void* stream);
+
+NOOR_MOE_API void noor_moe_destroy(noor_moe_handle* h);
+
+/* ---- expert-parallel communicator (NCCL over NVLink / NVSwitch) ---- */
+
+/* Size in bytes of the opaque unique id (NCCL_UNIQUE_ID_BYTES). */
+NOOR_MOE_API int noor_moe_comm_id_size(void);
+/* Rank 0 creates the id and ships it to the other ranks out of band. */
+NOOR_MOE_API int noor_moe_comm_get_id(void* id_out);
+/* Collective over world_size ranks; call with the handle's device current. */
+NOOR_MOE_API int noor_moe_comm_init_rank(const void* id, int world_size, int rank, int device, void** comm_out);
+NOOR_MOE_API int noor_moe_comm_destroy(void* comm);
+
+/* Plan of one expert-parallel exchange, from this rank's per-expert counts
+ * counts_local [E] and the counts every rank sent for this rank's experts
+ * counts_recv [G][E/G].  Outputs, per peer rank r: send_rows/send_off (rows of
+ * the expert-ordered send buffer bound for r) and recv_rows/recv_off (rows
+ * arriving from r); and the receive-side grouped-GEMM table of G*E/G groups,
+ * group j = (source rank j / (E/G), local expert j % (E/G)): grp_row [G*El+1]
+ * (first row), grp_mtile [G*El+1] (first BM-row tile), grp_widx [G*El+1]
+ * (local expert).  Pure host arithmetic; the library uses it inside
+ * noor_moe_forward and exports it for hosts that run their own transport. */
+NOOR_MOE_API int noor_moe_ep_plan(const int64_t* counts_local, const int64_t* counts_recv, int E, int G, int BM,
+                                  int64_t* send_rows, int64_t* send_off, int64_t* recv_rows, int64_t* recv_off,
+                                  int32_t* grp_row, int32_t* grp_mtile, int32_t* grp_widx);
+
+/* ---- measurement hooks (CUDA events on the launching stream) ---- */
+
+/* Begin recording a start/stop event pair around every kernel the handle
+ * launches, for at most `max_launches` launches. */
+NOOR_MOE_API int noor_moe_profile_begin(noor_moe_handle* h, int max_launches);
+/* Stop recording, synchronise, and fill per-kernel totals.  names is a buffer
+ * of n_slots * 32 chars (NUL-terminated names), total_ms / launches have
+ * n_slots entries.  Returns the number of distinct kernels in *n_out. */
+NOOR_MOE_API int noor_moe_profile_end(noor_moe_handle* h, char* names, float* total_ms, int32_t* launches,
+                         int n_slots, int* n_out);
+/* Number of kernels this handle has launched since creation. */
+NOOR_MOE_API int64_t noor_moe_launch_count(const noor_moe_handle* h);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NOOR_MOE_H */

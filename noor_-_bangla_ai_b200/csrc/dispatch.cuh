@@ -1,0 +1,206 @@
+// dispatch.cuh -- segment scan, K2 permute (dispatch) and K4 gather-combine.
+//
+// The reference dispatches one token at a time (moe.rs:150-165): for every
+// token it runs each selected expert on a 1-row tensor and accumulates
+// out[s] += w_i * expert_i(x_s) in rank order.  Here the dispatch is a
+// permutation: every (token, slot) pick gets a row in a buffer where the
+// picks of each expert are contiguous, so the experts run as one grouped
+// GEMM; the combine then gathers each token's k expert rows back in rank
+// order and adds the dense branch (parallel_ffn.rs:30-36).
+#pragma once
+
+#include "common.cuh"
+
+namespace noor {
+namespace dispatch {
+
+// ------------------------------------------------------------------ scan
+
+// One block.  From the per-token-block histograms hist[nblk][E]:
+//   counts[e]       = picks of expert e (int64, the API's utilization counts)
+//   seg_start[e]    = first row of expert e's segment (exclusive scan), [E+1]
+//   blk_base[b][e]  = first row of block b's picks of expert e
+//   mtile_start[e]  = first BM-row tile of expert e in the grouped GEMM, [E+1]
+// Expert segments are laid out in expert order; under expert parallelism the
+// experts of each rank are contiguous, so the rows bound for each rank are too.
+constexpr int kScanThreads = 1024;
+
+__global__ void __launch_bounds__(kScanThreads) scan_segments_kernel(const int32_t* __restrict__ hist, int32_t nblk,
+                                                                     int32_t E, int32_t BM,
+                                                                     int64_t* __restrict__ counts,
+                                                                     int32_t* __restrict__ seg_start,
+                                                                     int32_t* __restrict__ blk_base,
+                                                                     int32_t* __restrict__ mtile_start) {
+  extern __shared__ int32_t s_part[];  // [E][C]
+  __shared__ int32_t s_seg[1025];
+  const int C = max(1, kScanThreads / E);  // chunks per expert
+  const int chunk = (nblk + C - 1) / C;
+  const int e = threadIdx.x / C;
+  const int c = threadIdx.x - e * C;
+  const bool active = e < E;
+  const int b0 = c * chunk, b1 = min(nblk, b0 + chunk);
+  int sum = 0;
+  if (active)
+    for (int b = b0; b < b1; ++b) sum += hist[(int64_t)b * E + e];
+  if (active) s_part[e * C + c] = sum;
+  __syncthreads();
+  if (threadIdx.x < E) {
+    const int ee = threadIdx.x;
+    int run = 0;
+    for (int cc = 0; cc < C; ++cc) {
+      const int v = s_part[ee * C + cc];
+      s_part[ee * C + cc] = run;
+      run += v;
+    }
+    s_seg[ee] = run;  // total for expert ee (scanned below)
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0, tiles = 0;
+    for (int ee = 0; ee < E; ++ee) {
+      const int v = s_seg[ee];
+      counts[ee] = v;
+      seg_start[ee] = run;
+      mtile_start[ee] = tiles;
+      s_seg[ee] = run;
+      run += v;
+      tiles += (v + BM - 1) / BM;
+    }
+    seg_start[E] = run;
+    mtile_start[E] = tiles;
+  }
+  __syncthreads();
+  if (active) {
+    int run = s_seg[e] + s_part[e * C + c];
+    for (int b = b0; b < b1; ++b) {
+      blk_base[(int64_t)b * E + e] = run;
+      run += hist[(int64_t)b * E + e];
+    }
+  }
+}
+
+// ------------------------------------------------------------------ permute
+
+// One warp per token: read the token's row once with 16-byte loads and write
+// it to the row of each of its k picks; record that row in dst_row[t, slot].
+constexpr int kPermuteWarps = 8;
+
+__global__ void __launch_bounds__(kPermuteWarps * 32) permute_rows_kernel(
+    const uint8_t* __restrict__ x, int32_t row_bytes, int32_t T, int32_t k, int32_t E, int32_t tpb,
+    const int32_t* __restrict__ idx, const int32_t* __restrict__ lrank, const int32_t* __restrict__ blk_base,
+    uint8_t* __restrict__ xp, int32_t* __restrict__ dst_row) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int32_t t = blockIdx.x * kPermuteWarps + warp;
+  if (t >= T) return;
+  int32_t dst[8];
+  const int32_t* bb = blk_base + (int64_t)(t / tpb) * E;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (i < k) {
+      const int32_t e = __ldg(idx + (int64_t)t * k + i);
+      dst[i] = __ldg(bb + e) + __ldg(lrank + (int64_t)t * k + i);
+      if (lane == 0) dst_row[(int64_t)t * k + i] = dst[i];
+    }
+  }
+  const int nvec = row_bytes >> 4;
+  const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)t * row_bytes);
+  constexpr int U = 4;
+  for (int base = lane; base < nvec; base += 32 * U) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (base + 32 * u < nvec) v[u] = __ldg(src + base + 32 * u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i < k) {
+        uint4* d = reinterpret_cast<uint4*>(xp + (int64_t)dst[i] * row_bytes);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (base + 32 * u < nvec) d[base + 32 * u] = v[u];
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ combine
+
+// out[t] = (dense[t] + sum_i w[t,i] * y[dst_row[t,i]] (+ shared[t])) * 1/sqrt(2)
+// with the sum taken in rank order starting from zero and every multiply and
+// add rounded separately (moe.rs:159-173, parallel_ffn.rs:32-35).  Without a
+// dense branch the result is the MoE sum alone (MoELayer::forward).
+// YT / OUT: bf16 or float.  dense and shared are f32 (nullable).
+template <typename T_>
+struct Vec8;
+template <>
+struct Vec8<bf16> {
+  __device__ static void load(const bf16* p, float (&v)[8]) {
+    const uint4 r = *reinterpret_cast<const uint4*>(p);
+    v[0] = bf16_lo(r.x); v[1] = bf16_hi(r.x); v[2] = bf16_lo(r.y); v[3] = bf16_hi(r.y);
+    v[4] = bf16_lo(r.z); v[5] = bf16_hi(r.z); v[6] = bf16_lo(r.w); v[7] = bf16_hi(r.w);
+  }
+  __device__ static void store(bf16* p, const float (&v)[8]) {
+    *reinterpret_cast<uint4*>(p) =
+        make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
+  }
+};
+template <>
+struct Vec8<float> {
+  __device__ static void load(const float* p, float (&v)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+  __device__ static void store(float* p, const float (&v)[8]) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+  }
+};
+
+constexpr int kCombineWarps = 8;
+
+template <typename YT, typename OT>
+__global__ void __launch_bounds__(kCombineWarps * 32) combine_kernel(
+    const YT* __restrict__ y, const int32_t* __restrict__ dst_row, const float* __restrict__ wts,
+    const float* __restrict__ dense, const float* __restrict__ shared, int32_t T, int32_t d, int32_t k,
+    OT* __restrict__ out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int32_t t = blockIdx.x * kCombineWarps + warp;
+  if (t >= T) return;
+  int32_t rows[8];
+  float w[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (i < k) {
+      rows[i] = __ldg(dst_row + (int64_t)t * k + i);
+      w[i] = __ldg(wts + (int64_t)t * k + i);
+    }
+  const float inv_sqrt2 = 0x1.6a09e6p-1f;  // 1.0f32 / 2.0f32.sqrt() = 0.70710677
+  for (int c = lane * 8; c < d; c += 32 * 8) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i < k) {
+        float v[8];
+        Vec8<YT>::load(y + (int64_t)rows[i] * d + c, v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], __fmul_rn(w[i], v[j]));
+      }
+    }
+    if (shared) {
+      float v[8];
+      Vec8<float>::load(shared + (int64_t)t * d + c, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], v[j]);
+    }
+    if (dense) {
+      float v[8];
+      Vec8<float>::load(dense + (int64_t)t * d + c, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = __fmul_rn(__fadd_rn(v[j], acc[j]), inv_sqrt2);
+    }
+    Vec8<OT>::store(out + (int64_t)t * d + c, acc);
+  }
+}
+
+}  // namespace dispatch
+}  // namespace noor

@@ -1,0 +1,1101 @@
+// noor_moe.cu -- C ABI, handle, weight prepack and per-call orchestration of
+// the B200 sparse-MoE layer forward.
+//
+// One call of noor_moe_forward runs, on the caller's stream:
+//   K1  router            x -> top-k idx / weights, per-block ranks + histogram
+//   scan                  histograms -> expert segments, per-block bases, GEMM tile table
+//   K2  permute           x rows -> expert-contiguous rows (dst_row per pick)
+//   [EP] count exchange + all-to-all-v of the rows (NCCL send/recv), so each
+//        rank holds the rows of its own experts
+//   K3  expert GEMM 1     rows . [Wg|Wu]^T  -> silu(g)*u      (tcgen05, SwiGLU epilogue)
+//   K3  expert GEMM 2     h . Wd^T          -> y
+//   [EP] reverse all-to-all-v of y
+//   dense branch          x . [Wg|Wu]^T -> gelu(g)*u -> . Wd^T   (second stream)
+//   K4  combine           out = (dense + sum_i w_i y_i) / sqrt(2)
+// which is ParallelFFN::forward (crates/noor-core/src/layers/parallel_ffn.rs:30-36)
+// over MoELayer::forward (moe.rs:145-177).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "noor_moe.h"
+
+#include "common.cuh"
+#include "dispatch.cuh"
+#include "nccl_dyn.h"
+#include "prepack.cuh"
+#include "router.cuh"
+#include "simt_gemm.cuh"
+#include "tc_gemm.cuh"
+
+using namespace noor;
+
+// ============================================================== errors
+
+static thread_local std::string g_last_error;
+
+static int fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define CK(call)                                                                                       \
+  do {                                                                                                 \
+    cudaError_t e_ = (call);                                                                           \
+    if (e_ != cudaSuccess)                                                                             \
+      return fail(e_ == cudaErrorMemoryAllocation ? NOOR_MOE_ERR_OOM : NOOR_MOE_ERR_CUDA,              \
+                  "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__);                \
+  } while (0)
+
+#define CKN(call)                                                                                      \
+  do {                                                                                                 \
+    if (!noor::nccl().ok) return fail(NOOR_MOE_ERR_NCCL, "libnccl.so.2 could not be loaded");          \
+    ncclResult_t r_ = (call);                                                                          \
+    if (r_ != ncclSuccess)                                                                             \
+      return fail(NOOR_MOE_ERR_NCCL, "%s: %s (%s:%d)", #call, noor::nccl().GetErrorString(r_),         \
+                  __FILE__, __LINE__);                                                                 \
+  } while (0)
+
+#define CKR(call)               \
+  do {                          \
+    int rc_ = (call);           \
+    if (rc_ != NOOR_MOE_OK) return rc_; \
+  } while (0)
+
+// ============================================================== device buffers
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  int ensure(size_t n) {
+    if (n <= bytes) return NOOR_MOE_OK;
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+    if (n == 0) return NOOR_MOE_OK;
+    CK(cudaMalloc(&p, n));
+    bytes = n;
+    return NOOR_MOE_OK;
+  }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+  }
+  template <typename T>
+  T* as() const { return reinterpret_cast<T*>(p); }
+};
+
+// ============================================================== tensor maps
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 2-D K-major bf16 operand [rows, K] (row stride K elements), box BK x box_rows,
+// 128-byte swizzle (the UMMA K-major SW128 layout).
+static int encode_kmajor(CUtensorMap* m, const void* base, int64_t rows, int64_t K, int box_rows) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return fail(NOOR_MOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return fail(NOOR_MOE_ERR_INVALID, "tensor-core operand must be 16-byte aligned");
+  if ((K * 2) % 16 != 0) return fail(NOOR_MOE_ERR_INVALID, "row stride must be a multiple of 16 bytes");
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)std::max<int64_t>(rows, 1)};
+  cuuint64_t strides[1] = {(cuuint64_t)(K * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)tc::BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NOOR_MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return NOOR_MOE_OK;
+}
+
+// ============================================================== profiling
+
+enum KernelKind : int {
+  K_ROUTER = 0, K_ROUTER_SCORES, K_ROUTER_TOPK, K_SCAN, K_PERMUTE, K_EXPERT_GEMM1, K_EXPERT_GEMM2,
+  K_DENSE_GEMM1, K_DENSE_GEMM2, K_SHARED_GEMM1, K_SHARED_GEMM2, K_COMBINE, K_PREPACK, K_A2A_DISPATCH,
+  K_A2A_COMBINE, K_COUNT_EXCHANGE, K_MATMUL, K_NUM
+};
+static const char* kKindNames[K_NUM] = {
+    "router", "router_scores", "router_topk", "scan", "permute", "expert_gemm1", "expert_gemm2",
+    "dense_gemm1", "dense_gemm2", "shared_gemm1", "shared_gemm2", "combine", "prepack",
+    "a2a_dispatch", "a2a_combine", "count_exchange", "matmul"};
+
+// ============================================================== handle
+
+struct noor_moe_handle {
+  noor_moe_desc desc{};
+  int E = 0, k = 0, d = 0, ff = 0, dff = 0, G = 1, rank = 0, El = 0, e0 = 0;
+  bool bf16 = true;
+  int dev = 0, num_sms = 148;
+  ncclComm_t comm = nullptr;
+  bool comm_broken = false;
+  bool weights = false;
+
+  // router
+  DevBuf gate, bias, scales;  // gate: bf16 [Epad][d] (BF16) or f32 [d][E] (F32)
+  int Epad = 0;
+  // experts (local), dense, shared
+  DevBuf w1, w2;                  // BF16 packed
+  DevBuf wg32, wu32, wd32;        // F32 reference layout
+  DevBuf dw1, dw2, dg32, du32, dd32;
+  DevBuf sw1, sw2, sg32, su32, sd32;
+  bool has_shared = false, has_dense = false;
+  CUtensorMap tm_w1{}, tm_w2{}, tm_dw1{}, tm_dw2{}, tm_sw1{}, tm_sw2{};
+  int bn2 = 256;  // n-tile of GEMMs whose N is d
+
+  // workspaces
+  int64_t capT = 0;
+  DevBuf x_in, out_buf, idx, wts, lrank, dst_row, blk_hist, blk_base, counts64, counts_glob, seg_start, mtile_start;
+  DevBuf scores;
+  DevBuf xp, h, y, xrecv, ysend;
+  DevBuf dense_h, dense_out, shared_h, shared_out;
+  DevBuf grp_row, grp_mtile, grp_widx, cnt_recv;
+  int64_t* h_cnt = nullptr;  // pinned [E + G*El]
+  int32_t* h_grp = nullptr;  // pinned [3 * (G*El + 1)]
+  CUtensorMap tm_xp{}, tm_xrecv{}, tm_h{}, tm_xin{}, tm_dh{}, tm_sh{};
+
+  cudaStream_t own = nullptr, aux = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_done = nullptr;
+  int* d_err = nullptr;
+
+  // profiling
+  bool prof_on = false;
+  int prof_cap = 0, prof_used = 0;
+  std::vector<cudaEvent_t> prof_ev;
+  std::vector<int> prof_kind;
+  int64_t launches = 0;
+};
+
+extern "C" int noor_moe_ep_plan(const int64_t* counts_local, const int64_t* counts_recv, int E, int G, int BM,
+                                int64_t* send_rows, int64_t* send_off, int64_t* recv_rows, int64_t* recv_off,
+                                int32_t* grp_row, int32_t* grp_mtile, int32_t* grp_widx) {
+  if (!counts_local || !counts_recv || E <= 0 || G <= 0 || E % G != 0 || BM <= 0)
+    return fail(NOOR_MOE_ERR_INVALID, "bad plan arguments");
+  const int El = E / G;
+  int64_t so = 0, ro = 0;
+  for (int r = 0; r < G; ++r) {
+    int64_t sr = 0, rr = 0;
+    for (int le = 0; le < El; ++le) {
+      if (counts_local[r * El + le] < 0 || counts_recv[r * El + le] < 0)
+        return fail(NOOR_MOE_ERR_INVALID, "negative count");
+      sr += counts_local[r * El + le];
+      rr += counts_recv[r * El + le];
+    }
+    send_rows[r] = sr;
+    send_off[r] = so;
+    recv_rows[r] = rr;
+    recv_off[r] = ro;
+    so += sr;
+    ro += rr;
+  }
+  if (ro > INT32_MAX) return fail(NOOR_MOE_ERR_INVALID, "received rows overflow");
+  int64_t r0 = 0, t0 = 0;
+  for (int src = 0; src < G; ++src)
+    for (int le = 0; le < El; ++le) {
+      const int j = src * El + le;
+      const int64_t c = counts_recv[j];
+      grp_row[j] = (int32_t)r0;
+      grp_mtile[j] = (int32_t)t0;
+      grp_widx[j] = le;
+      r0 += c;
+      t0 += (c + BM - 1) / BM;
+    }
+  grp_row[G * El] = (int32_t)r0;
+  grp_mtile[G * El] = (int32_t)t0;
+  grp_widx[G * El] = 0;
+  return NOOR_MOE_OK;
+}
+
+namespace {
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+// Launch wrapper: brackets the launch with profile events when enabled and
+// counts it.
+template <typename F>
+int launch(noor_moe_handle* h, cudaStream_t s, int kind, F&& f) {
+  const bool prof = h->prof_on && h->prof_used < h->prof_cap;
+  if (prof) CK(cudaEventRecord(h->prof_ev[2 * h->prof_used], s));
+  f();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(NOOR_MOE_ERR_CUDA, "launch of %s failed: %s", kKindNames[kind], cudaGetErrorString(e));
+  if (prof) {
+    CK(cudaEventRecord(h->prof_ev[2 * h->prof_used + 1], s));
+    h->prof_kind[h->prof_used] = kind;
+    ++h->prof_used;
+  }
+  ++h->launches;
+  return NOOR_MOE_OK;
+}
+
+// Like launch() for NCCL phases (not counted as kernels of this library).
+template <typename F>
+int timed_phase(noor_moe_handle* h, cudaStream_t s, int kind, F&& f) {
+  const bool prof = h->prof_on && h->prof_used < h->prof_cap;
+  if (prof) CK(cudaEventRecord(h->prof_ev[2 * h->prof_used], s));
+  CKR(f());
+  if (prof) {
+    CK(cudaEventRecord(h->prof_ev[2 * h->prof_used + 1], s));
+    h->prof_kind[h->prof_used] = kind;
+    ++h->prof_used;
+  }
+  return NOOR_MOE_OK;
+}
+
+int wait_event_deadline(noor_moe_handle* h, cudaEvent_t ev, double seconds) {
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    cudaError_t q = cudaEventQuery(ev);
+    if (q == cudaSuccess) return NOOR_MOE_OK;
+    if (q != cudaErrorNotReady) return fail(NOOR_MOE_ERR_CUDA, "stream failed: %s", cudaGetErrorString(q));
+    const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (el > seconds) {
+      if (h->comm) {
+        noor::nccl().CommAbort(h->comm);  // releases NCCL kernels waiting for a lost peer
+        h->comm = nullptr;
+        h->comm_broken = true;
+        return fail(NOOR_MOE_ERR_NCCL, "expert-parallel exchange did not finish within %.0f s; "
+                    "communicator aborted", seconds);
+      }
+      return fail(NOOR_MOE_ERR_TIMEOUT, "device work did not finish within %.0f s", seconds);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+int check_device_error(noor_moe_handle* h) {
+  int err = 0;
+  CK(cudaMemcpy(&err, h->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err != 0) {
+    cudaMemset(h->d_err, 0, sizeof(int));
+    return fail(NOOR_MOE_ERR_TIMEOUT, "a kernel's bounded wait gave up (device code %d)", err);
+  }
+  return NOOR_MOE_OK;
+}
+
+int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
+
+// ============================================================== workspaces
+
+int ensure_workspace(noor_moe_handle* h, int64_t T) {
+  if (T <= h->capT) return NOOR_MOE_OK;
+  const int64_t capT = round_up(std::max<int64_t>(T, h->desc.max_tokens), 128);
+  const int64_t b = h->bf16 ? 2 : 4;
+  const int64_t Rl = capT * h->k;           // picks made on this rank
+  const int64_t Rr = Rl * h->G;             // worst-case rows received under EP
+  const int64_t nblk = (capT + 63) / 64;    // smallest token block is 64
+  const int64_t d = h->d;
+  CKR(h->x_in.ensure(capT * d * b));
+  CKR(h->out_buf.ensure(capT * d * b));
+  CKR(h->idx.ensure(Rl * 4));
+  CKR(h->wts.ensure(Rl * 4));
+  CKR(h->lrank.ensure(Rl * 4));
+  CKR(h->dst_row.ensure(Rl * 4));
+  CKR(h->blk_hist.ensure(nblk * h->E * 4));
+  CKR(h->blk_base.ensure(nblk * h->E * 4));
+  CKR(h->counts64.ensure(h->E * 8));
+  CKR(h->counts_glob.ensure(h->E * 8));
+  CKR(h->seg_start.ensure((h->E + 1) * 4));
+  CKR(h->mtile_start.ensure((h->E + 1) * 4));
+  if (!h->bf16) CKR(h->scores.ensure(capT * h->E * 4));
+  CKR(h->xp.ensure(Rl * d * b));
+  CKR(h->h.ensure(Rr * h->ff * b));
+  CKR(h->y.ensure(Rr * d * b));
+  if (h->G > 1) {
+    CKR(h->xrecv.ensure(Rr * d * b));
+    CKR(h->ysend.ensure(Rl * d * b));
+    const int ng = h->G * h->El;
+    CKR(h->grp_row.ensure((ng + 1) * 4));
+    CKR(h->grp_mtile.ensure((ng + 1) * 4));
+    CKR(h->grp_widx.ensure((ng + 1) * 4));
+    CKR(h->cnt_recv.ensure(ng * 8));
+  }
+  if (h->has_dense) {
+    CKR(h->dense_h.ensure(capT * h->dff * b));
+    CKR(h->dense_out.ensure(capT * d * 4));
+  }
+  if (h->has_shared) {
+    CKR(h->shared_h.ensure(capT * h->ff * b));
+    CKR(h->shared_out.ensure(capT * d * 4));
+  }
+  if (h->bf16) {
+    CKR(encode_kmajor(&h->tm_xp, h->xp.p, Rl, d, tc::BM));
+    if (h->G > 1) CKR(encode_kmajor(&h->tm_xrecv, h->xrecv.p, Rr, d, tc::BM));
+    CKR(encode_kmajor(&h->tm_h, h->h.p, Rr, h->ff, tc::BM));
+    CKR(encode_kmajor(&h->tm_xin, h->x_in.p, capT, d, tc::BM));
+    if (h->has_dense) CKR(encode_kmajor(&h->tm_dh, h->dense_h.p, capT, h->dff, tc::BM));
+    if (h->has_shared) CKR(encode_kmajor(&h->tm_sh, h->shared_h.p, capT, h->ff, tc::BM));
+  }
+  h->capT = capT;
+  return NOOR_MOE_OK;
+}
+
+// ============================================================== GEMM launchers
+
+template <int BN, int EPI>
+int launch_tc(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& tA, const CUtensorMap& tB,
+              const GroupTable& gt, int N, int K, void* C, int64_t ldc, int64_t max_mtiles) {
+  using Cf = tc::Cfg<BN>;
+  auto kern = tc::grouped_gemm_kernel<BN, EPI>;
+  CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM_BYTES));
+  tc::Params p;
+  p.groups = gt;
+  p.N = N;
+  p.K = K;
+  p.n_tiles = N / BN;
+  p.C = C;
+  p.ldc = ldc;
+  p.err = h->d_err;
+  const int64_t tiles = std::max<int64_t>(1, max_mtiles * p.n_tiles);
+  const int grid = (int)std::min<int64_t>(h->num_sms, tiles);
+  return launch(h, s, kind, [&] { kern<<<grid, tc::NUM_THREADS, Cf::SMEM_BYTES, s>>>(tA, tB, p); });
+}
+
+template <int EPI>
+int launch_simt(noor_moe_handle* h, cudaStream_t s, int kind, const GroupTable& gt, const float* A, int64_t lda,
+                const float* Bg, const float* Bu, int64_t b_stride, int N, int K, float* C, int64_t ldc,
+                int64_t max_mtiles) {
+  simt::Params p;
+  p.groups = gt;
+  p.A = A;
+  p.lda = lda;
+  p.Bg = Bg;
+  p.Bu = Bu;
+  p.b_stride = b_stride;
+  p.N = N;
+  p.K = K;
+  p.n_tiles = (N + simt::BN - 1) / simt::BN;
+  p.C = C;
+  p.ldc = ldc;
+  const int64_t tiles = std::max<int64_t>(1, max_mtiles * p.n_tiles);
+  const int grid = (int)std::min<int64_t>((int64_t)h->num_sms * 8, tiles);
+  return launch(h, s, kind, [&] { simt::grouped_gemm_f32_kernel<EPI><<<grid, simt::THREADS, 0, s>>>(p); });
+}
+
+GroupTable dense_group(int64_t rows) {
+  GroupTable g;
+  g.row_start = g.mtile_start = g.weight_idx = nullptr;
+  g.G = 1;
+  g.dense_rows = (int32_t)rows;
+  return g;
+}
+
+// GLU FFN over `rows` rows of A: out = act(A.Wg) * (A.Wu) . Wd.
+// BF16: tensor cores (tA is A's map); F32: CUDA cores.
+int run_glu_ffn(noor_moe_handle* h, cudaStream_t s, int kind1, int kind2, const CUtensorMap* tA, const void* A,
+                int64_t rows, int ffn, int act_silu, const CUtensorMap* tW1, const CUtensorMap* tW2, const CUtensorMap* tH,
+                const float* g32, const float* u32, const float* d32, void* hbuf, float* out) {
+  const GroupTable gt = dense_group(rows);
+  const int d = h->d;
+  if (h->bf16) {
+    const int64_t mt = (rows + tc::BM - 1) / tc::BM;
+    if (act_silu)
+      CKR((launch_tc<256, tc::EPI_SWIGLU_BF16>(h, s, kind1, *tA, *tW1, gt, 2 * ffn, d, hbuf, ffn, mt)));
+    else
+      CKR((launch_tc<256, tc::EPI_GEGLU_BF16>(h, s, kind1, *tA, *tW1, gt, 2 * ffn, d, hbuf, ffn, mt)));
+    if (h->bn2 == 256)
+      CKR((launch_tc<256, tc::EPI_STORE_F32>(h, s, kind2, *tH, *tW2, gt, d, ffn, out, d, mt)));
+    else
+      CKR((launch_tc<128, tc::EPI_STORE_F32>(h, s, kind2, *tH, *tW2, gt, d, ffn, out, d, mt)));
+  } else {
+    const int64_t mt = (rows + simt::BM - 1) / simt::BM;
+    if (act_silu)
+      CKR((launch_simt<simt::EPI_SWIGLU>(h, s, kind1, gt, (const float*)A, d, g32, u32, 0, ffn, d, (float*)hbuf, ffn, mt)));
+    else
+      CKR((launch_simt<simt::EPI_GEGLU>(h, s, kind1, gt, (const float*)A, d, g32, u32, 0, ffn, d, (float*)hbuf, ffn, mt)));
+    CKR((launch_simt<simt::EPI_STORE>(h, s, kind2, gt, (const float*)hbuf, ffn, d32, nullptr, 0, d, ffn, out, d, mt)));
+  }
+  return NOOR_MOE_OK;
+}
+
+// ============================================================== router
+
+// Launch K1 and the scan.  Fills idx, wts, lrank, blk_hist, counts64,
+// seg_start, blk_base, mtile_start.  Returns the token-block size in *tpb.
+int run_router(noor_moe_handle* h, cudaStream_t s, const void* x, int64_t T, int* tpb_out) {
+  router::RouterOut ro{h->idx.as<int32_t>(), h->wts.as<float>(), h->lrank.as<int32_t>(), h->blk_hist.as<int32_t>()};
+  const int E = h->E, k = h->k, d = h->d;
+  int tpb = 0;
+  if (h->bf16) {
+    const int NF = h->Epad / 8;
+    const int MF = NF <= 8 ? 2 : 1;
+    tpb = 64 * MF;
+    const int nblk = (int)((T + tpb - 1) / tpb);
+    const bf16* xg = reinterpret_cast<const bf16*>(x);
+    const bf16* gt = h->gate.as<bf16>();
+    const float* b = h->bias.as<float>();
+    const float* sc = h->scales.as<float>();
+#define NOOR_ROUTE_CASE(NF_, MF_)                                                                          \
+  case NF_:                                                                                                \
+    CKR(launch(h, s, K_ROUTER, [&] {                                                                       \
+      router::route_bf16_kernel<NF_, MF_><<<nblk, 128, 0, s>>>(xg, gt, b, sc, (int32_t)T, d, E, k, ro);    \
+    }));                                                                                                   \
+    break;
+    switch (NF) {
+      NOOR_ROUTE_CASE(1, 2) NOOR_ROUTE_CASE(2, 2) NOOR_ROUTE_CASE(3, 2) NOOR_ROUTE_CASE(4, 2)
+      NOOR_ROUTE_CASE(5, 2) NOOR_ROUTE_CASE(6, 2) NOOR_ROUTE_CASE(7, 2) NOOR_ROUTE_CASE(8, 2)
+      NOOR_ROUTE_CASE(9, 1) NOOR_ROUTE_CASE(10, 1) NOOR_ROUTE_CASE(11, 1) NOOR_ROUTE_CASE(12, 1)
+      NOOR_ROUTE_CASE(13, 1) NOOR_ROUTE_CASE(14, 1) NOOR_ROUTE_CASE(15, 1) NOOR_ROUTE_CASE(16, 1)
+      default:
+        return fail(NOOR_MOE_ERR_UNSUPPORTED, "tensor-core router supports at most 128 experts");
+    }
+#undef NOOR_ROUTE_CASE
+    CKR(launch(h, s, K_SCAN, [&] {
+      const int C = std::max(1, dispatch::kScanThreads / E);
+      dispatch::scan_segments_kernel<<<1, dispatch::kScanThreads, E * C * 4, s>>>(
+          h->blk_hist.as<int32_t>(), nblk, E, tc::BM, h->counts64.as<int64_t>(), h->seg_start.as<int32_t>(),
+          h->blk_base.as<int32_t>(), h->mtile_start.as<int32_t>());
+    }));
+  } else {
+    tpb = router::kTopkTPB;
+    const int nblk = (int)((T + tpb - 1) / tpb);
+    const int64_t n = T * E;
+    CKR(launch(h, s, K_ROUTER_SCORES, [&] {
+      router::route_f32_scores_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+          (const float*)x, h->gate.as<float>(), h->bias.as<float>(), (int32_t)T, d, E, h->scores.as<float>());
+    }));
+    const size_t smem = (size_t)(k * tpb / 32) * E * 4;
+    CKR(launch(h, s, K_ROUTER_TOPK, [&] {
+      router::topk_from_scores_kernel<<<nblk, router::kTopkTPB, smem, s>>>(h->scores.as<float>(), h->scales.as<float>(),
+                                                                           (int32_t)T, E, k, ro);
+    }));
+    CKR(launch(h, s, K_SCAN, [&] {
+      const int C = std::max(1, dispatch::kScanThreads / E);
+      dispatch::scan_segments_kernel<<<1, dispatch::kScanThreads, E * C * 4, s>>>(
+          h->blk_hist.as<int32_t>(), nblk, E, simt::BM, h->counts64.as<int64_t>(), h->seg_start.as<int32_t>(),
+          h->blk_base.as<int32_t>(), h->mtile_start.as<int32_t>());
+    }));
+  }
+  *tpb_out = tpb;
+  return NOOR_MOE_OK;
+}
+
+// ============================================================== expert parallel exchange
+
+ncclDataType_t act_nccl_type(const noor_moe_handle* h) { return h->bf16 ? ncclBfloat16 : ncclFloat32; }
+
+struct EpPlan {
+  std::vector<int64_t> send_rows, send_off, recv_rows, recv_off;
+  int64_t recv_total = 0;
+  int64_t mtiles = 0;
+};
+
+// Exchange per-expert counts, then build the receive-side group table with
+// noor_moe_ep_plan (group j = (source rank, local expert), rows contiguous in
+// xrecv, weight index = local expert).
+int ep_plan(noor_moe_handle* h, cudaStream_t s, EpPlan& plan) {
+  const int G = h->G, El = h->El, E = h->E;
+  CKR(timed_phase(h, s, K_COUNT_EXCHANGE, [&]() -> int {
+    CKN(noor::nccl().GroupStart());
+    for (int r = 0; r < G; ++r) {
+      CKN(noor::nccl().Send(h->counts64.as<int64_t>() + (int64_t)r * El, El, ncclInt64, r, h->comm, s));
+      CKN(noor::nccl().Recv(h->cnt_recv.as<int64_t>() + (int64_t)r * El, El, ncclInt64, r, h->comm, s));
+    }
+    CKN(noor::nccl().GroupEnd());
+    return NOOR_MOE_OK;
+  }));
+  CK(cudaMemcpyAsync(h->h_cnt, h->counts64.p, E * 8, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(h->h_cnt + E, h->cnt_recv.p, (int64_t)G * El * 8, cudaMemcpyDeviceToHost, s));
+  CK(cudaEventRecord(h->ev_done, s));
+  CKR(wait_event_deadline(h, h->ev_done, 120.0));
+  plan.send_rows.assign(G, 0);
+  plan.send_off.assign(G, 0);
+  plan.recv_rows.assign(G, 0);
+  plan.recv_off.assign(G, 0);
+  const int ng = G * El;
+  int32_t* row = h->h_grp;
+  int32_t* mt = h->h_grp + (ng + 1);
+  int32_t* wi = h->h_grp + 2 * (ng + 1);
+  const int BM = h->bf16 ? tc::BM : simt::BM;
+  CKR(noor_moe_ep_plan(h->h_cnt, h->h_cnt + E, E, G, BM, plan.send_rows.data(), plan.send_off.data(),
+                       plan.recv_rows.data(), plan.recv_off.data(), row, mt, wi));
+  plan.recv_total = row[ng];
+  plan.mtiles = mt[ng];
+  CK(cudaMemcpyAsync(h->grp_row.p, row, (ng + 1) * 4, cudaMemcpyHostToDevice, s));
+  CK(cudaMemcpyAsync(h->grp_mtile.p, mt, (ng + 1) * 4, cudaMemcpyHostToDevice, s));
+  CK(cudaMemcpyAsync(h->grp_widx.p, wi, (ng + 1) * 4, cudaMemcpyHostToDevice, s));
+  return NOOR_MOE_OK;
+}
+
+int ep_exchange(noor_moe_handle* h, cudaStream_t s, int kind, const EpPlan& plan, const void* sendbuf,
+                void* recvbuf, bool reverse) {
+  const int64_t row_elems = h->d;
+  const int64_t b = h->bf16 ? 2 : 4;
+  return timed_phase(h, s, kind, [&]() -> int {
+    CKN(noor::nccl().GroupStart());
+    for (int r = 0; r < h->G; ++r) {
+      const int64_t sr = reverse ? plan.recv_rows[r] : plan.send_rows[r];
+      const int64_t so = reverse ? plan.recv_off[r] : plan.send_off[r];
+      const int64_t rr = reverse ? plan.send_rows[r] : plan.recv_rows[r];
+      const int64_t ro = reverse ? plan.send_off[r] : plan.recv_off[r];
+      if (sr > 0)
+        CKN(noor::nccl().Send(static_cast<const uint8_t*>(sendbuf) + so * row_elems * b, sr * row_elems, act_nccl_type(h), r,
+                     h->comm, s));
+      if (rr > 0)
+        CKN(noor::nccl().Recv(static_cast<uint8_t*>(recvbuf) + ro * row_elems * b, rr * row_elems, act_nccl_type(h), r,
+                     h->comm, s));
+    }
+    CKN(noor::nccl().GroupEnd());
+    return NOOR_MOE_OK;
+  });
+}
+
+// ============================================================== forward
+
+// x, out: device pointers of the layer dtype.  tmx: tensor map of x (BF16).
+int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtensorMap* tmx, void* out, int64_t T) {
+  const int d = h->d, k = h->k, E = h->E;
+  const int64_t b = h->bf16 ? 2 : 4;
+
+  // Dense / shared branches depend only on x: fork them onto the aux stream.
+  const bool side = (h->has_dense || h->has_shared) && T > 0;
+  if (side) {
+    CK(cudaEventRecord(h->ev_fork, s));
+    CK(cudaStreamWaitEvent(h->aux, h->ev_fork, 0));
+    if (h->has_dense)
+      CKR(run_glu_ffn(h, h->aux, K_DENSE_GEMM1, K_DENSE_GEMM2, tmx, x, T, h->dff, h->desc.dense_act == NOOR_ACT_SILU,
+                      &h->tm_dw1, &h->tm_dw2, &h->tm_dh, h->dg32.as<float>(), h->du32.as<float>(), h->dd32.as<float>(),
+                      h->dense_h.p, h->dense_out.as<float>()));
+    if (h->has_shared)
+      CKR(run_glu_ffn(h, h->aux, K_SHARED_GEMM1, K_SHARED_GEMM2, tmx, x, T, h->ff, 1, &h->tm_sw1, &h->tm_sw2,
+                      &h->tm_sh, h->sg32.as<float>(), h->su32.as<float>(), h->sd32.as<float>(), h->shared_h.p,
+                      h->shared_out.as<float>()));
+    CK(cudaEventRecord(h->ev_join, h->aux));
+  }
+
+  int tpb = 0;
+  if (T == 0) {
+    // A rank with no tokens still takes part in the exchange with zero counts.
+    CK(cudaMemsetAsync(h->counts64.p, 0, E * 8, s));
+  } else {
+    CKR(run_router(h, s, x, T, &tpb));
+  }
+  if (T > 0) CKR(launch(h, s, K_PERMUTE, [&] {
+    const unsigned grid = (unsigned)((T + dispatch::kPermuteWarps - 1) / dispatch::kPermuteWarps);
+    dispatch::permute_rows_kernel<<<grid, dispatch::kPermuteWarps * 32, 0, s>>>(
+        static_cast<const uint8_t*>(x), (int32_t)(d * b), (int32_t)T, k, E, tpb, h->idx.as<int32_t>(),
+        h->lrank.as<int32_t>(), h->blk_base.as<int32_t>(), h->xp.as<uint8_t>(), h->dst_row.as<int32_t>());
+  }));
+
+  GroupTable gt;
+  const CUtensorMap* tA = &h->tm_xp;
+  const void* A32 = h->xp.p;
+  int64_t max_mtiles = 0;
+  void* ybuf = h->y.p;  // rows the combine gathers from
+  EpPlan plan;
+  if (h->G == 1) {
+    gt.row_start = h->seg_start.as<int32_t>();
+    gt.mtile_start = h->mtile_start.as<int32_t>();
+    gt.weight_idx = nullptr;
+    gt.G = E;
+    gt.dense_rows = -1;
+    const int BM = h->bf16 ? tc::BM : simt::BM;
+    max_mtiles = (T * k + BM - 1) / BM + E;
+  } else {
+    CKR(ep_plan(h, s, plan));
+    CKR(ep_exchange(h, s, K_A2A_DISPATCH, plan, h->xp.p, h->xrecv.p, false));
+    gt.row_start = h->grp_row.as<int32_t>();
+    gt.mtile_start = h->grp_mtile.as<int32_t>();
+    gt.weight_idx = h->grp_widx.as<int32_t>();
+    gt.G = h->G * h->El;
+    gt.dense_rows = -1;
+    tA = &h->tm_xrecv;
+    A32 = h->xrecv.p;
+    max_mtiles = plan.mtiles;
+    ybuf = h->ysend.p;
+  }
+
+  if (max_mtiles > 0) {
+    if (h->bf16) {
+      CKR((launch_tc<256, tc::EPI_SWIGLU_BF16>(h, s, K_EXPERT_GEMM1, *tA, h->tm_w1, gt, 2 * h->ff, d, h->h.p, h->ff,
+                                               max_mtiles)));
+      if (h->bn2 == 256)
+        CKR((launch_tc<256, tc::EPI_STORE_BF16>(h, s, K_EXPERT_GEMM2, h->tm_h, h->tm_w2, gt, d, h->ff, h->y.p, d,
+                                                max_mtiles)));
+      else
+        CKR((launch_tc<128, tc::EPI_STORE_BF16>(h, s, K_EXPERT_GEMM2, h->tm_h, h->tm_w2, gt, d, h->ff, h->y.p, d,
+                                                max_mtiles)));
+    } else {
+      const int64_t ffd = (int64_t)d * h->ff;
+      CKR((launch_simt<simt::EPI_SWIGLU>(h, s, K_EXPERT_GEMM1, gt, (const float*)A32, d, h->wg32.as<float>(),
+                                         h->wu32.as<float>(), ffd, h->ff, d, h->h.as<float>(), h->ff, max_mtiles)));
+      CKR((launch_simt<simt::EPI_STORE>(h, s, K_EXPERT_GEMM2, gt, h->h.as<float>(), h->ff, h->wd32.as<float>(), nullptr,
+                                        ffd, d, h->ff, h->y.as<float>(), d, max_mtiles)));
+    }
+  }
+  if (h->G > 1) CKR(ep_exchange(h, s, K_A2A_COMBINE, plan, h->y.p, h->ysend.p, true));
+
+  if (side) CK(cudaStreamWaitEvent(s, h->ev_join, 0));
+  if (T > 0) CKR(launch(h, s, K_COMBINE, [&] {
+    const unsigned grid = (unsigned)((T + dispatch::kCombineWarps - 1) / dispatch::kCombineWarps);
+    const float* dense = h->has_dense ? h->dense_out.as<float>() : nullptr;
+    const float* shared = h->has_shared ? h->shared_out.as<float>() : nullptr;
+    if (h->bf16)
+      dispatch::combine_kernel<bf16, bf16><<<grid, dispatch::kCombineWarps * 32, 0, s>>>(
+          (const bf16*)ybuf, h->dst_row.as<int32_t>(), h->wts.as<float>(), dense, shared, (int32_t)T, d, k,
+          (bf16*)out);
+    else
+      dispatch::combine_kernel<float, float><<<grid, dispatch::kCombineWarps * 32, 0, s>>>(
+          (const float*)ybuf, h->dst_row.as<int32_t>(), h->wts.as<float>(), dense, shared, (int32_t)T, d, k,
+          (float*)out);
+  }));
+  return NOOR_MOE_OK;
+}
+
+int global_counts(noor_moe_handle* h, cudaStream_t s, const int64_t** src) {
+  if (h->G == 1) {
+    *src = h->counts64.as<int64_t>();
+    return NOOR_MOE_OK;
+  }
+  CKN(noor::nccl().AllReduce(h->counts64.p, h->counts_glob.p, h->E, ncclInt64, ncclSum, h->comm, s));
+  *src = h->counts_glob.as<int64_t>();
+  return NOOR_MOE_OK;
+}
+
+int validate(const noor_moe_desc* d) {
+  if (!d) return fail(NOOR_MOE_ERR_INVALID, "null descriptor");
+  if (d->d_model <= 0 || d->n_experts <= 0 || d->top_k <= 0 || d->expert_ff <= 0)
+    return fail(NOOR_MOE_ERR_INVALID, "sizes must be positive");
+  if (d->dtype != NOOR_DTYPE_F32 && d->dtype != NOOR_DTYPE_BF16) return fail(NOOR_MOE_ERR_INVALID, "unknown dtype");
+  if (d->dense_act != NOOR_ACT_GELU_TANH && d->dense_act != NOOR_ACT_SILU)
+    return fail(NOOR_MOE_ERR_INVALID, "unknown dense activation");
+  if (d->has_dense && d->dense_ff <= 0) return fail(NOOR_MOE_ERR_INVALID, "dense_ff must be positive");
+  const int k = std::min(d->top_k, d->n_experts);
+  if (k > router::kMaxTopK) return fail(NOOR_MOE_ERR_UNSUPPORTED, "top_k > %d", router::kMaxTopK);
+  if (d->world_size < 1 || d->rank < 0 || d->rank >= d->world_size) return fail(NOOR_MOE_ERR_INVALID, "bad rank");
+  if (d->n_experts % d->world_size != 0)
+    return fail(NOOR_MOE_ERR_INVALID, "n_experts must be divisible by world_size");
+  if (d->d_model % 8 != 0) return fail(NOOR_MOE_ERR_UNSUPPORTED, "d_model must be a multiple of 8");
+  if (d->n_experts > 256) return fail(NOOR_MOE_ERR_UNSUPPORTED, "at most 256 experts");
+  if (d->dtype == NOOR_DTYPE_BF16) {
+    if (d->n_experts > router::kMaxExpertsTC)
+      return fail(NOOR_MOE_ERR_UNSUPPORTED, "BF16 layers support at most %d experts", router::kMaxExpertsTC);
+    if (d->d_model % 128 != 0 || d->expert_ff % 128 != 0 || (d->has_dense && d->dense_ff % 128 != 0))
+      return fail(NOOR_MOE_ERR_UNSUPPORTED, "BF16 layers need d_model, expert_ff, dense_ff multiples of 128");
+  }
+  return NOOR_MOE_OK;
+}
+
+}  // namespace
+
+// ============================================================== C ABI
+
+extern "C" {
+
+const char* noor_moe_last_error(void) { return g_last_error.c_str(); }
+
+int noor_moe_create(const noor_moe_desc* desc, void* nccl_comm, noor_moe_handle** out) {
+  if (!out) return fail(NOOR_MOE_ERR_INVALID, "null out");
+  *out = nullptr;
+  CKR(validate(desc));
+  if (desc->world_size > 1 && !nccl_comm)
+    return fail(NOOR_MOE_ERR_INVALID, "world_size > 1 needs an NCCL communicator");
+  int ndev = 0;
+  CK(cudaGetDeviceCount(&ndev));
+  if (desc->device < 0 || desc->device >= ndev) return fail(NOOR_MOE_ERR_INVALID, "bad device %d", desc->device);
+  DeviceGuard g(desc->device);
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, desc->device));
+  if (desc->dtype == NOOR_DTYPE_BF16 && prop.major != 10)
+    return fail(NOOR_MOE_ERR_UNSUPPORTED, "BF16 layers need an sm_100 GPU (found sm_%d%d)", prop.major, prop.minor);
+  noor_moe_handle* h = new noor_moe_handle();
+  h->desc = *desc;
+  h->E = desc->n_experts;
+  h->k = std::min(desc->top_k, desc->n_experts);
+  h->d = desc->d_model;
+  h->ff = desc->expert_ff;
+  h->dff = desc->dense_ff;
+  h->G = desc->world_size;
+  h->rank = desc->rank;
+  h->El = h->E / h->G;
+  h->e0 = h->rank * h->El;
+  h->bf16 = desc->dtype == NOOR_DTYPE_BF16;
+  h->dev = desc->device;
+  h->num_sms = prop.multiProcessorCount;
+  h->comm = static_cast<ncclComm_t>(nccl_comm);
+  h->has_dense = desc->has_dense != 0;
+  h->has_shared = desc->has_shared != 0;
+  h->Epad = (h->E + 7) / 8 * 8;
+  h->bn2 = (h->d % 256 == 0) ? 256 : 128;
+  auto bail = [&](int rc) {
+    noor_moe_destroy(h);
+    return rc;
+  };
+  if (cudaStreamCreateWithFlags(&h->own, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&h->aux, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&h->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&h->ev_join, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&h->ev_done, cudaEventDisableTiming) != cudaSuccess ||
+      cudaMalloc(&h->d_err, sizeof(int)) != cudaSuccess || cudaMemset(h->d_err, 0, sizeof(int)) != cudaSuccess)
+    return bail(fail(NOOR_MOE_ERR_CUDA, "stream/event/flag setup failed"));
+  if (h->G > 1) {
+    const int ng = h->G * h->El;
+    if (cudaMallocHost(&h->h_cnt, (h->E + ng) * 8) != cudaSuccess ||
+        cudaMallocHost(&h->h_grp, 3 * (ng + 1) * 4) != cudaSuccess)
+      return bail(fail(NOOR_MOE_ERR_OOM, "pinned host buffers"));
+  }
+  const int rc = ensure_workspace(h, std::max<int64_t>(desc->max_tokens, 128));
+  if (rc != NOOR_MOE_OK) return bail(rc);
+  *out = h;
+  return NOOR_MOE_OK;
+}
+
+int noor_moe_load_weights(noor_moe_handle* h, const float* gate, const float* bias, const float* scales,
+                          const float* const* w_gate, const float* const* w_up, const float* const* w_down,
+                          const float* const* shared, const float* const* dense) {
+  if (!h || !gate || !bias || !scales || !w_gate || !w_up || !w_down)
+    return fail(NOOR_MOE_ERR_INVALID, "null weight pointer");
+  if (h->has_dense && (!dense || !dense[0] || !dense[1] || !dense[2]))
+    return fail(NOOR_MOE_ERR_INVALID, "dense branch weights missing");
+  if (h->has_shared && (!shared || !shared[0] || !shared[1] || !shared[2]))
+    return fail(NOOR_MOE_ERR_INVALID, "shared expert weights missing");
+  for (int le = 0; le < h->El; ++le)
+    if (!w_gate[h->e0 + le] || !w_up[h->e0 + le] || !w_down[h->e0 + le])
+      return fail(NOOR_MOE_ERR_INVALID, "expert %d weights missing", h->e0 + le);
+  DeviceGuard g(h->dev);
+  const int d = h->d, ff = h->ff, dff = h->dff, E = h->E, El = h->El;
+  CKR(h->bias.ensure(E * 4));
+  CKR(h->scales.ensure(E * 4));
+  CK(cudaMemcpy(h->bias.p, bias, E * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(h->scales.p, scales, E * 4, cudaMemcpyHostToDevice));
+  cudaStream_t s = h->own;
+  if (!h->bf16) {
+    const int64_t m = (int64_t)d * ff;
+    CKR(h->gate.ensure((int64_t)d * E * 4));
+    CK(cudaMemcpy(h->gate.p, gate, (int64_t)d * E * 4, cudaMemcpyHostToDevice));
+    CKR(h->wg32.ensure(El * m * 4));
+    CKR(h->wu32.ensure(El * m * 4));
+    CKR(h->wd32.ensure(El * m * 4));
+    for (int le = 0; le < El; ++le) {
+      CK(cudaMemcpy(h->wg32.as<float>() + le * m, w_gate[h->e0 + le], m * 4, cudaMemcpyHostToDevice));
+      CK(cudaMemcpy(h->wu32.as<float>() + le * m, w_up[h->e0 + le], m * 4, cudaMemcpyHostToDevice));
+      CK(cudaMemcpy(h->wd32.as<float>() + le * m, w_down[h->e0 + le], m * 4, cudaMemcpyHostToDevice));
+    }
+    if (h->has_dense) {
+      const int64_t md = (int64_t)d * dff;
+      CKR(h->dg32.ensure(md * 4));
+      CKR(h->du32.ensure(md * 4));
+      CKR(h->dd32.ensure(md * 4));
+      CK(cudaMemcpy(h->dg32.p, dense[0], md * 4, cudaMemcpyHostToDevice));
+      CK(cudaMemcpy(h->du32.p, dense[1], md * 4, cudaMemcpyHostToDevice));
+      CK(cudaMemcpy(h->dd32.p, dense[2], md * 4, cudaMemcpyHostToDevice));
+    }
+    if (h->has_shared) {
+      CKR(h->sg32.ensure(m * 4));
+      CKR(h->su32.ensure(m * 4));
+      CKR(h->sd32.ensure(m * 4));
+      CK(cudaMemcpy(h->sg32.p, shared[0], m * 4, cudaMemcpyHostToDevice));
+      CK(cudaMemcpy(h->su32.p, shared[1], m * 4, cudaMemcpyHostToDevice));
+      CK(cudaMemcpy(h->sd32.p, shared[2], m * 4, cudaMemcpyHostToDevice));
+    }
+    CK(cudaDeviceSynchronize());
+    h->weights = true;
+    return NOOR_MOE_OK;
+  }
+
+  // BF16: stage each f32 matrix on the device, then transpose + round.
+  const int64_t stage_elems = std::max<int64_t>({(int64_t)d * ff, (int64_t)d * std::max(dff, 1), (int64_t)d * E});
+  DevBuf stage;
+  CKR(stage.ensure(stage_elems * 4));
+  auto pack = [&](const float* src, int K, int N, bf16* dst, int group, int stride, int offset) -> int {
+    CK(cudaMemcpyAsync(stage.p, src, (int64_t)K * N * 4, cudaMemcpyHostToDevice, s));
+    dim3 grid((N + 31) / 32, (K + 31) / 32), block(32, 8);
+    CKR(launch(h, s, K_PREPACK, [&] {
+      prepack::transpose_to_bf16_kernel<<<grid, block, 0, s>>>(stage.as<float>(), K, N, dst, K, group, stride, offset);
+    }));
+    CK(cudaStreamSynchronize(s));  // the staging buffer is reused by the next matrix
+    return NOOR_MOE_OK;
+  };
+  CKR(h->gate.ensure((int64_t)h->Epad * d * 2));
+  CK(cudaMemset(h->gate.p, 0, (int64_t)h->Epad * d * 2));
+  CKR(pack(gate, d, E, h->gate.as<bf16>(), E, E, 0));
+  // experts: W1 [El][2ff][d] with 128-row gate / up blocks interleaved; W2 [El][d][ff]
+  CKR(h->w1.ensure((int64_t)El * 2 * ff * d * 2));
+  CKR(h->w2.ensure((int64_t)El * d * ff * 2));
+  for (int le = 0; le < El; ++le) {
+    bf16* w1 = h->w1.as<bf16>() + (int64_t)le * 2 * ff * d;
+    CKR(pack(w_gate[h->e0 + le], d, ff, w1, 128, 256, 0));
+    CKR(pack(w_up[h->e0 + le], d, ff, w1, 128, 256, 128));
+    CKR(pack(w_down[h->e0 + le], ff, d, h->w2.as<bf16>() + (int64_t)le * d * ff, d, d, 0));
+  }
+  CKR(encode_kmajor(&h->tm_w1, h->w1.p, (int64_t)El * 2 * ff, d, 256));
+  CKR(encode_kmajor(&h->tm_w2, h->w2.p, (int64_t)El * d, ff, h->bn2));
+  if (h->has_dense) {
+    CKR(h->dw1.ensure((int64_t)2 * dff * d * 2));
+    CKR(h->dw2.ensure((int64_t)d * dff * 2));
+    CKR(pack(dense[0], d, dff, h->dw1.as<bf16>(), 128, 256, 0));
+    CKR(pack(dense[1], d, dff, h->dw1.as<bf16>(), 128, 256, 128));
+    CKR(pack(dense[2], dff, d, h->dw2.as<bf16>(), d, d, 0));
+    CKR(encode_kmajor(&h->tm_dw1, h->dw1.p, 2 * dff, d, 256));
+    CKR(encode_kmajor(&h->tm_dw2, h->dw2.p, d, dff, h->bn2));
+  }
+  if (h->has_shared) {
+    CKR(h->sw1.ensure((int64_t)2 * ff * d * 2));
+    CKR(h->sw2.ensure((int64_t)d * ff * 2));
+    CKR(pack(shared[0], d, ff, h->sw1.as<bf16>(), 128, 256, 0));
+    CKR(pack(shared[1], d, ff, h->sw1.as<bf16>(), 128, 256, 128));
+    CKR(pack(shared[2], ff, d, h->sw2.as<bf16>(), d, d, 0));
+    CKR(encode_kmajor(&h->tm_sw1, h->sw1.p, 2 * ff, d, 256));
+    CKR(encode_kmajor(&h->tm_sw2, h->sw2.p, d, ff, h->bn2));
+  }
+  stage.release();
+  h->weights = true;
+  return NOOR_MOE_OK;
+}
+
+int noor_moe_set_bias(noor_moe_handle* h, const float* bias) {
+  if (!h || !bias) return fail(NOOR_MOE_ERR_INVALID, "null argument");
+  if (!h->weights) return fail(NOOR_MOE_ERR_STATE, "set_bias before load_weights");
+  DeviceGuard g(h->dev);
+  CK(cudaMemcpy(h->bias.p, bias, h->E * 4, cudaMemcpyHostToDevice));
+  return NOOR_MOE_OK;
+}
+
+static int forward_impl(noor_moe_handle* h, const void* x, void* out, int64_t T, int32_t* topk_idx, float* topk_w,
+                        int64_t* expert_counts, void* stream, bool route_only) {
+  if (!h) return fail(NOOR_MOE_ERR_INVALID, "null handle");
+  if (!h->weights) return fail(NOOR_MOE_ERR_STATE, "forward before load_weights");
+  if (h->comm_broken) return fail(NOOR_MOE_ERR_STATE, "communicator was aborted after a failed exchange");
+  if (T < 0 || T > (int64_t)INT32_MAX / std::max(1, h->k * h->G))
+    return fail(NOOR_MOE_ERR_INVALID, "token count %lld out of range", (long long)T);
+  if (!x && T > 0) return fail(NOOR_MOE_ERR_INVALID, "null x");
+  if (!route_only && !out && T > 0) return fail(NOOR_MOE_ERR_INVALID, "null out");
+  DeviceGuard g(h->dev);
+  CKR(ensure_workspace(h, std::max<int64_t>(T, 1)));
+  const bool host = stream == nullptr;
+  cudaStream_t s = host ? h->own : static_cast<cudaStream_t>(stream);
+  const int64_t b = h->bf16 ? 2 : 4;
+  const int64_t xbytes = T * h->d * b;
+  if (T == 0 && h->G == 1) {
+    if (expert_counts) {
+      if (host) std::memset(expert_counts, 0, h->E * 8);
+      else CK(cudaMemsetAsync(expert_counts, 0, h->E * 8, s));
+    }
+    return NOOR_MOE_OK;
+  }
+  const void* xd = x;
+  const CUtensorMap* tmx = &h->tm_xin;
+  CUtensorMap tm_user;
+  if (host) {
+    if (T > 0) CK(cudaMemcpyAsync(h->x_in.p, x, xbytes, cudaMemcpyHostToDevice, s));
+    xd = h->x_in.p;
+  } else if (h->bf16 && !route_only && (h->has_dense || h->has_shared)) {
+    CKR(encode_kmajor(&tm_user, x, T, h->d, tc::BM));
+    tmx = &tm_user;
+  }
+  if (route_only) {
+    int tpb = 0;
+    if (T > 0) CKR(run_router(h, s, xd, T, &tpb));
+  } else {
+    void* od = host ? h->out_buf.p : out;
+    CKR(run_forward(h, s, xd, tmx, od, T));
+    if (host && T > 0) CK(cudaMemcpyAsync(out, od, xbytes, cudaMemcpyDeviceToHost, s));
+  }
+  const cudaMemcpyKind dk = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+  if (topk_idx && T > 0) CK(cudaMemcpyAsync(topk_idx, h->idx.p, T * h->k * 4, dk, s));
+  if (topk_w && T > 0) CK(cudaMemcpyAsync(topk_w, h->wts.p, T * h->k * 4, dk, s));
+  if (expert_counts) {
+    const int64_t* src = nullptr;
+    if (route_only || h->G == 1) src = h->counts64.as<int64_t>();
+    else CKR(global_counts(h, s, &src));
+    CK(cudaMemcpyAsync(expert_counts, src, h->E * 8, dk, s));
+  }
+  if (host) {
+    CK(cudaEventRecord(h->ev_done, s));
+    CKR(wait_event_deadline(h, h->ev_done, 300.0));
+    CKR(check_device_error(h));
+  }
+  return NOOR_MOE_OK;
+}
+
+int noor_moe_forward(noor_moe_handle* h, const void* x, void* out, int64_t T, int32_t* topk_idx, float* topk_w,
+                     int64_t* expert_counts, void* stream) {
+  return forward_impl(h, x, out, T, topk_idx, topk_w, expert_counts, stream, false);
+}
+
+int noor_moe_route(noor_moe_handle* h, const void* x, int64_t T, int32_t* idx, float* w, int64_t* counts,
+                   void* stream) {
+  if (!idx || !w) return fail(NOOR_MOE_ERR_INVALID, "idx and w are required");
+  return forward_impl(h, x, nullptr, T, idx, w, counts, stream, true);
+}
+
+int noor_moe_sync(noor_moe_handle* h, void* stream) {
+  if (!h) return fail(NOOR_MOE_ERR_INVALID, "null handle");
+  DeviceGuard g(h->dev);
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->own;
+  CK(cudaEventRecord(h->ev_done, s));
+  CKR(wait_event_deadline(h, h->ev_done, 300.0));
+  return check_device_error(h);
+}
+
+void noor_moe_destroy(noor_moe_handle* h) {
+  if (!h) return;
+  {
+    DeviceGuard g(h->dev);
+    cudaDeviceSynchronize();
+    DevBuf* bufs[] = {&h->gate, &h->bias, &h->scales, &h->w1, &h->w2, &h->wg32, &h->wu32, &h->wd32, &h->dw1,
+                      &h->dw2, &h->dg32, &h->du32, &h->dd32, &h->sw1, &h->sw2, &h->sg32, &h->su32, &h->sd32,
+                      &h->x_in, &h->out_buf, &h->idx, &h->wts, &h->lrank, &h->dst_row, &h->blk_hist,
+                      &h->blk_base, &h->counts64, &h->counts_glob, &h->seg_start, &h->mtile_start, &h->scores,
+                      &h->xp, &h->h, &h->y, &h->xrecv, &h->ysend, &h->dense_h, &h->dense_out, &h->shared_h,
+                      &h->shared_out, &h->grp_row, &h->grp_mtile, &h->grp_widx, &h->cnt_recv};
+    for (DevBuf* b : bufs) b->release();
+    if (h->h_cnt) cudaFreeHost(h->h_cnt);
+    if (h->h_grp) cudaFreeHost(h->h_grp);
+    if (h->d_err) cudaFree(h->d_err);
+    for (cudaEvent_t e : h->prof_ev) cudaEventDestroy(e);
+    if (h->ev_fork) cudaEventDestroy(h->ev_fork);
+    if (h->ev_join) cudaEventDestroy(h->ev_join);
+    if (h->ev_done) cudaEventDestroy(h->ev_done);
+    if (h->own) cudaStreamDestroy(h->own);
+    if (h->aux) cudaStreamDestroy(h->aux);
+  }
+  delete h;
+}
+
+int noor_matmul_f32(const float* a, const float* b, float* c, int64_t m, int64_t k, int64_t n) {
+  if (!a || !b || !c) return fail(NOOR_MOE_ERR_INVALID, "null argument");
+  if (m <= 0 || k <= 0 || n <= 0 || m > INT32_MAX || k > INT32_MAX || n > INT32_MAX)
+    return fail(NOOR_MOE_ERR_INVALID, "bad shape");
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, dev));
+  DevBuf A, B, C;
+  CKR(A.ensure(m * k * 4));
+  CKR(B.ensure(k * n * 4));
+  CKR(C.ensure(m * n * 4));
+  CK(cudaMemcpy(A.p, a, m * k * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(B.p, b, k * n * 4, cudaMemcpyHostToDevice));
+  simt::Params p;
+  p.groups = dense_group(m);
+  p.A = A.as<float>();
+  p.lda = k;
+  p.Bg = B.as<float>();
+  p.Bu = nullptr;
+  p.b_stride = 0;
+  p.N = (int32_t)n;
+  p.K = (int32_t)k;
+  p.n_tiles = (int32_t)((n + simt::BN - 1) / simt::BN);
+  p.C = C.as<float>();
+  p.ldc = n;
+  const int64_t tiles = (m + simt::BM - 1) / simt::BM * p.n_tiles;
+  const int grid = (int)std::min<int64_t>((int64_t)prop.multiProcessorCount * 8, tiles);
+  simt::grouped_gemm_f32_kernel<simt::EPI_STORE><<<grid, simt::THREADS>>>(p);
+  CK(cudaGetLastError());
+  CK(cudaMemcpy(c, C.p, m * n * 4, cudaMemcpyDeviceToHost));
+  return NOOR_MOE_OK;
+}
+
+int noor_moe_comm_id_size(void) { return (int)sizeof(ncclUniqueId); }
+
+int noor_moe_comm_get_id(void* id_out) {
+  if (!id_out) return fail(NOOR_MOE_ERR_INVALID, "null id");
+  ncclUniqueId id;
+  CKN(noor::nccl().GetUniqueId(&id));
+  std::memcpy(id_out, &id, sizeof(id));
+  return NOOR_MOE_OK;
+}
+
+int noor_moe_comm_init_rank(const void* id, int world_size, int rank, int device, void** comm_out) {
+  if (!id || !comm_out) return fail(NOOR_MOE_ERR_INVALID, "null argument");
+  DeviceGuard g(device);
+  ncclUniqueId uid;
+  std::memcpy(&uid, id, sizeof(uid));
+  ncclComm_t comm;
+  CKN(noor::nccl().CommInitRank(&comm, world_size, uid, rank));
+  *comm_out = comm;
+  return NOOR_MOE_OK;
+}
+
+int noor_moe_comm_destroy(void* comm) {
+  if (!comm) return NOOR_MOE_OK;
+  CKN(noor::nccl().CommDestroy(static_cast<ncclComm_t>(comm)));
+  return NOOR_MOE_OK;
+}
+
+int noor_moe_profile_begin(noor_moe_handle* h, int max_launches) {
+  if (!h || max_launches <= 0) return fail(NOOR_MOE_ERR_INVALID, "bad argument");
+  DeviceGuard g(h->dev);
+  while ((int)h->prof_ev.size() < 2 * max_launches) {
+    cudaEvent_t e;
+    CK(cudaEventCreate(&e));
+    h->prof_ev.push_back(e);
+  }
+  h->prof_kind.assign(max_launches, 0);
+  h->prof_cap = max_launches;
+  h->prof_used = 0;
+  h->prof_on = true;
+  return NOOR_MOE_OK;
+}
+
+int noor_moe_profile_end(noor_moe_handle* h, char* names, float* total_ms, int32_t* launches, int n_slots,
+                         int* n_out) {
+  if (!h || !names || !total_ms || !launches || !n_out) return fail(NOOR_MOE_ERR_INVALID, "null argument");
+  DeviceGuard g(h->dev);
+  h->prof_on = false;
+  float tot[K_NUM] = {0};
+  int cnt[K_NUM] = {0};
+  for (int i = 0; i < h->prof_used; ++i) {
+    CK(cudaEventSynchronize(h->prof_ev[2 * i + 1]));
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, h->prof_ev[2 * i], h->prof_ev[2 * i + 1]));
+    tot[h->prof_kind[i]] += ms;
+    cnt[h->prof_kind[i]] += 1;
+  }
+  int n = 0;
+  for (int kd = 0; kd < K_NUM && n < n_slots; ++kd) {
+    if (!cnt[kd]) continue;
+    std::snprintf(names + 32 * n, 32, "%s", kKindNames[kd]);
+    total_ms[n] = tot[kd];
+    launches[n] = cnt[kd];
+    ++n;
+  }
+  *n_out = n;
+  h->prof_used = 0;
+  return NOOR_MOE_OK;
+}
+
+int64_t noor_moe_launch_count(const noor_moe_handle* h) { return h ? h->launches : 0; }
+
+}  // extern "C"

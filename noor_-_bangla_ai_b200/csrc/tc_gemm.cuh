@@ -1,0 +1,390 @@
+// tc_gemm.cuh -- grouped BF16 GEMM on sm_100a tensor cores (tcgen05 + TMA).
+//
+// C[rows of group g, :] = epilogue( A[rows of g, :K] . B[weight_idx[g]]^T )
+//
+// A is [rows, K] bf16 row-major (K-major); B holds one [N, K] bf16 K-major
+// matrix per weight index (the library prepacks the reference's [K, N]
+// row-major weights transposed).  This one kernel runs all four GEMMs of the
+// layer: the expert gate/up projection with the SwiGLU epilogue, the expert
+// down projection, and the dense branch's gate/up (GeGLU epilogue) and down
+// projections (crates/noor-core/src/layers/ffn.rs:24-34, 62-68).
+//
+// Design (one persistent CTA per SM, warp-specialised):
+//   warp 0 lane 0 : TMA producer, STAGES-deep ring of (A, B) k-blocks in smem
+//   warp 1 lane 0 : tcgen05.mma issuer, M=128 x N=BN x K=16 per instruction,
+//                   f32 accumulator in TMEM, double-buffered (2 x BN columns)
+//   warps 2..5    : epilogue, tcgen05.ld TMEM -> registers -> activation ->
+//                   global; warp w reads TMEM lanes 32*(w%4) .. +31
+// Every mbarrier wait is bounded: after kWaitLimitCycles it records an error
+// code in the handle's device error word, raises a CTA-wide abort flag, and
+// all roles leave their loops; TMEM is always released before exit.
+//
+// No TMA multicast is used anywhere: every CTA loads its own tiles.
+#pragma once
+
+#include <cuda.h>
+#include "common.cuh"
+
+namespace noor {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes = one 128B swizzle row
+constexpr int STAGES = 4;
+constexpr int NUM_THREADS = 192;
+
+enum Epilogue : int {
+  EPI_STORE_BF16 = 0,   // C = acc (bf16)
+  EPI_STORE_F32 = 1,    // C = acc (f32)
+  EPI_SWIGLU_BF16 = 2,  // C[:, j] = silu(acc[:, j]) * acc[:, BN/2 + j]   (per n-tile)
+  EPI_GEGLU_BF16 = 3,   // C[:, j] = gelu_tanh(acc[:, j]) * acc[:, BN/2 + j]
+};
+
+__host__ __device__ constexpr bool epi_gated(int e) { return e == EPI_SWIGLU_BF16 || e == EPI_GEGLU_BF16; }
+
+template <int BN>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
+  static constexpr uint32_t TMEM_COLS = 2 * BN;                    // two accumulators
+  // Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A bf16 (bits 7-9 = 1),
+  // B bf16 (bits 10-12 = 1), both K-major (bits 15/16 = 0), N>>3 at bit 17,
+  // M>>4 at bit 24.
+  static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) |
+                                    ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
+  static_assert(TMEM_COLS <= 512, "TMEM holds 512 columns");
+};
+
+struct Params {
+  GroupTable groups;
+  int32_t N;        // columns of each weight matrix (rows of B per weight index)
+  int32_t K;
+  int32_t n_tiles;  // N / BN
+  void* C;
+  int64_t ldc;      // elements
+  int* err;         // device error word
+};
+
+// ---------------------------------------------------------------- PTX helpers
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity to complete.  Returns
+// false (after recording `code`) if the CTA is aborting or the limit passed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long start = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - start > kWaitLimitCycles) {
+      *abort_flag = 1;
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x,
+                                            int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major operand laid out by TMA with
+// 128-byte swizzle: rows of 128 bytes, 8-row atoms 1024 bytes apart (SBO),
+// LBO unused for swizzled K-major (encoded 1), version 1 (bit 46),
+// layout SWIZZLE_128B (2 at bits 61-63).  The atom base must be 1024-aligned.
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 lanes x 32 consecutive f32 columns: thread i of the warp gets lane
+// (base lane + i), columns col .. col+31.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------- epilogue
+
+template <int EPI>
+__device__ __forceinline__ void store_chunk32(void* C, int64_t ldc, int row, int col, const uint32_t (&v)[32],
+                                              const uint32_t (&u)[32]) {
+  if constexpr (EPI == EPI_STORE_F32) {
+    float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(C) + (int64_t)row * ldc + col);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      dst[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                           __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+  } else {
+    uint32_t p[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float a = __uint_as_float(v[2 * j]), b = __uint_as_float(v[2 * j + 1]);
+      if constexpr (EPI == EPI_SWIGLU_BF16) {
+        a = __fmul_rn(act_silu(a), __uint_as_float(u[2 * j]));
+        b = __fmul_rn(act_silu(b), __uint_as_float(u[2 * j + 1]));
+      } else if constexpr (EPI == EPI_GEGLU_BF16) {
+        a = __fmul_rn(act_gelu_tanh(a), __uint_as_float(u[2 * j]));
+        b = __fmul_rn(act_gelu_tanh(b), __uint_as_float(u[2 * j + 1]));
+      }
+      p[j] = pack_bf16(a, b);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(C) + (int64_t)row * ldc + col);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+  }
+}
+
+// ---------------------------------------------------------------- kernel
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const Params p) {
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;                        // STAGES x A_BYTES
+  uint8_t* smB = smem + STAGES * C::A_BYTES;  // STAGES x B_BYTES
+
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t accf_bar[2];
+  __shared__ __align__(8) uint64_t acce_bar[2];
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&accf_bar[a], 1);
+      mbar_init(&acce_bar[a], 4);  // one arrive per epilogue warp
+    }
+    mbar_init(&drain_bar, 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_slot)),
+                 "r"(C::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+
+  const int32_t total_tiles = group_total_mtiles(p.groups, BM) * p.n_tiles;
+  const int32_t num_kb = (p.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+    // ---------------- TMA producer
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int32_t tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+      const TileCoord tc = decode_tile(p.groups, tile, p.n_tiles, BM);
+      const int32_t brow = tc.widx * p.N + tc.nt * BN;
+      bool ok = true;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, &abort_flag, p.err, DEV_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
+        tma_load_2d(smA + stage * C::A_BYTES, &tmA, &full_bar[stage], kb * BK, tc.row0);
+        tma_load_2d(smB + stage * C::B_BYTES, &tmB, &full_bar[stage], kb * BK, brow);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+    }
+    }
+    __syncwarp();  // lanes 1..31 wait here so the warp reaches the block barrier converged
+  } else if (warp == 1) {
+    if (lane == 0) {
+    // ---------------- MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool issued = false;
+    for (int32_t tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+      if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1u, &abort_flag, p.err, DEV_TIMEOUT_MMA)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+      bool ok = true;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, &abort_flag, p.err, DEV_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_addr(smA + stage * C::A_BYTES);
+        const uint32_t b0 = smem_addr(smB + stage * C::B_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          // advance 16 bf16 (32 bytes) along K inside the 128-byte swizzle row
+          umma_bf16(d_tmem, sdesc_sw128(a0 + kk * 32), sdesc_sw128(b0 + kk * 32), C::IDESC,
+                    (kb | kk) != 0 ? 1u : 0u);
+        }
+        issued = true;
+        umma_commit(&empty_bar[stage]);  // frees the smem stage once these MMAs retire
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      umma_commit(&accf_bar[acc]);  // accumulator ready for the epilogue
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (issued) {
+      // Retire every MMA this thread issued before TMEM is released.
+      umma_commit(&drain_bar);
+      const long long start = clock64();
+      while (!mbar_try_wait(&drain_bar, 0) && clock64() - start < kWaitLimitCycles) {
+      }
+    }
+    }
+    __syncwarp();
+  } else if (warp >= 2) {
+    // ---------------- epilogue: warp w owns TMEM lanes 32*(w%4) .. +31
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int32_t tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+      const TileCoord tc = decode_tile(p.groups, tile, p.n_tiles, BM);
+      if (!mbar_wait(&accf_bar[acc], acc_phase, &abort_flag, p.err, DEV_TIMEOUT_EPILOGUE)) break;
+      tc_fence_after();
+      const uint32_t t_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      const bool valid = row_in_tile < tc.rows;
+      const int row = tc.row0 + row_in_tile;
+      if constexpr (epi_gated(EPI)) {
+        constexpr int HALF = BN / 2;
+#pragma unroll 1
+        for (int c = 0; c < HALF; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld32(t_base + c, g);
+          tmem_ld32(t_base + HALF + c, u);
+          tmem_ld_wait();
+          if (valid) store_chunk32<EPI>(p.C, p.ldc, row, tc.nt * HALF + c, g, u);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t g[32];
+          tmem_ld32(t_base + c, g);
+          tmem_ld_wait();
+          if (valid) store_chunk32<EPI>(p.C, p.ldc, row, tc.nt * BN + c, g, g);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce_bar[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::TMEM_COLS)
+                 : "memory");
+  }
+#endif
+}
+
+}  // namespace tc
+}  // namespace noor

@@ -1,0 +1,276 @@
+"""ctypes front end of the CPU oracle, plus an independent numpy restatement.
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline leg, never by the library.  See noor_oracle.c for the
+reference lines each function restates (crates/noor-core/src/layers/moe.rs,
+ffn.rs, parallel_ffn.rs, tensor.rs; crates/noor-train/src/optim/smebu.rs).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from typing import Optional
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "libnoor_oracle.so")
+_lib = None
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i32p = ctypes.POINTER(ctypes.c_int32)
+_i64p = ctypes.POINTER(ctypes.c_int64)
+_f64p = ctypes.POINTER(ctypes.c_double)
+_i64 = ctypes.c_int64
+
+
+class _Layer(ctypes.Structure):
+    _fields_ = [
+        ("d_model", _i64), ("n_experts", _i64), ("top_k", _i64), ("expert_ff", _i64),
+        ("dense_ff", _i64),
+        ("gate", _f32p), ("bias", _f32p), ("scales", _f32p),
+        ("w_gate", _f32p), ("w_up", _f32p), ("w_down", _f32p),
+        ("shared_gate", _f32p), ("shared_up", _f32p), ("shared_down", _f32p),
+        ("dense_gate", _f32p), ("dense_up", _f32p), ("dense_down", _f32p),
+    ]
+
+
+def build() -> str:
+    """Compile libnoor_oracle.so with its Makefile (gcc, -ffp-contract=off)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH) or (
+                os.path.getmtime(_LIB_PATH) < os.path.getmtime(os.path.join(_HERE, "noor_oracle.c"))):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.noor_oracle_f32_to_bf16.restype = ctypes.c_uint16
+        L.noor_oracle_f32_to_bf16.argtypes = [ctypes.c_float]
+        L.noor_oracle_bf16_to_f32.restype = ctypes.c_float
+        L.noor_oracle_bf16_to_f32.argtypes = [ctypes.c_uint16]
+        L.noor_oracle_round_bf16.argtypes = [_f32p, _i64]
+        for name in ("sigmoid", "silu", "gelu"):
+            fn = getattr(L, "noor_oracle_" + name)
+            fn.restype = ctypes.c_float
+            fn.argtypes = [ctypes.c_float]
+        L.noor_oracle_use_openblas.restype = ctypes.c_int
+        L.noor_oracle_use_openblas.argtypes = [ctypes.c_char_p, ctypes.c_int]
+        L.noor_oracle_matmul.argtypes = [_f32p, _f32p, _f32p, _i64, _i64, _i64]
+        L.noor_oracle_route.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64, _i64,
+                                        _i32p, _f32p, _i64p, _f32p]
+        L.noor_oracle_scores_f64.argtypes = [_f32p, _f32p, _f32p, _i64, _i64, _i64, _f64p, _f64p]
+        L.noor_oracle_glu_ffn.argtypes = [_f32p, _i64, _i64, _i64, _f32p, _f32p, _f32p,
+                                          ctypes.c_int, _f32p]
+        L.noor_oracle_moe_forward.argtypes = [ctypes.POINTER(_Layer), _f32p, _i64, _f32p, _i32p,
+                                              _f32p, _i64p]
+        L.noor_oracle_parallel_forward.argtypes = L.noor_oracle_moe_forward.argtypes
+        L.noor_oracle_rms_norm.argtypes = [_f32p, _f32p, _i64, _i64, ctypes.c_double, _f32p]
+        L.noor_oracle_smebu_update.argtypes = [_f32p, _f32p, _f32p, _i64, ctypes.c_float,
+                                               ctypes.c_float, ctypes.c_float]
+        _lib = L
+    return _lib
+
+
+def _p(a: Optional[np.ndarray], t=_f32p):
+    if a is None:
+        return ctypes.cast(None, t)
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(t)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+# ---------------------------------------------------------------- scalar ops
+
+def f32_to_bf16(x: float) -> int:
+    return int(lib().noor_oracle_f32_to_bf16(x))
+
+
+def bf16_to_f32(h: int) -> float:
+    return float(lib().noor_oracle_bf16_to_f32(h))
+
+
+def round_bf16(a) -> np.ndarray:
+    a = _f32(a).copy()
+    lib().noor_oracle_round_bf16(_p(a), a.size)
+    return a
+
+
+def sigmoid(x: float) -> float:
+    return float(lib().noor_oracle_sigmoid(x))
+
+
+def silu(x: float) -> float:
+    return float(lib().noor_oracle_silu(x))
+
+
+def gelu(x: float) -> float:
+    return float(lib().noor_oracle_gelu(x))
+
+
+def use_openblas(threads: int = 0) -> bool:
+    """Route oracle matmuls through numpy's bundled ILP64 OpenBLAS sgemm (the
+    reference's cblas route, kernels.rs:151-163).  Returns False if absent."""
+    libs = os.path.join(os.path.dirname(np.__file__) + ".libs")
+    if not os.path.isdir(libs):
+        libs = os.path.join(os.path.dirname(os.path.dirname(np.__file__)), "numpy.libs")
+    cands = [f for f in os.listdir(libs) if f.startswith("libscipy_openblas64_")] if os.path.isdir(libs) else []
+    if not cands:
+        return False
+    rc = lib().noor_oracle_use_openblas(os.path.join(libs, cands[0]).encode(), threads)
+    return rc == 0
+
+
+def use_plain_loops() -> None:
+    lib().noor_oracle_use_openblas(None, 0)
+
+
+# ---------------------------------------------------------------- layer ops
+
+def matmul(a, b) -> np.ndarray:
+    a, b = _f32(a), _f32(b)
+    m, k = a.shape
+    k2, n = b.shape
+    assert k == k2
+    c = np.empty((m, n), np.float32)
+    lib().noor_oracle_matmul(_p(a), _p(b), _p(c), m, k, n)
+    return c
+
+
+def route(x, gate, bias, scales, k: int, want_scores: bool = False):
+    """Batched MoERouter::route (moe.rs:79-107) + ExpertUtilization::record.
+    Returns idx [T,k] int32, w [T,k] f32, counts [E] int64 (and scores [T,E])."""
+    x, gate, bias, scales = _f32(x), _f32(gate), _f32(bias), _f32(scales)
+    T, d = x.shape
+    E = gate.shape[1]
+    kk = min(k, E)
+    idx = np.empty((T, kk), np.int32)
+    w = np.empty((T, kk), np.float32)
+    counts = np.zeros(E, np.int64)
+    scores = np.empty((T, E), np.float32) if want_scores else None
+    lib().noor_oracle_route(_p(x), _p(gate), _p(bias), _p(scales), T, d, E, k, _p(idx, _i32p),
+                            _p(w), _p(counts, _i64p), _p(scores))
+    if want_scores:
+        return idx, w, counts, scores
+    return idx, w, counts
+
+
+def scores_f64(x, gate, bias):
+    """Router scores with f64 accumulation and the absolute-sum bound."""
+    x, gate, bias = _f32(x), _f32(gate), _f32(bias)
+    T, d = x.shape
+    E = gate.shape[1]
+    s = np.empty((T, E), np.float64)
+    ab = np.empty((T, E), np.float64)
+    lib().noor_oracle_scores_f64(_p(x), _p(gate), _p(bias), T, d, E, _p(s, _f64p), _p(ab, _f64p))
+    return s, ab
+
+
+def glu_ffn(x, w_gate, w_up, w_down, act: int) -> np.ndarray:
+    """act 0 = GeGLUFFN::forward (ffn.rs:24-34), 1 = SwiGLUFFN::forward (ffn.rs:62-68)."""
+    x, w_gate, w_up, w_down = _f32(x), _f32(w_gate), _f32(w_up), _f32(w_down)
+    m, d = x.shape
+    ff = w_gate.shape[1]
+    out = np.empty((m, d), np.float32)
+    lib().noor_oracle_glu_ffn(_p(x), m, d, ff, _p(w_gate), _p(w_up), _p(w_down), act, _p(out))
+    return out
+
+
+def _layer_struct(w, top_k: int):
+    d, E = w.gate.shape
+    ff = w.w_gate.shape[2]
+    dff = w.dense_gate.shape[1]
+    keep = [w.gate, w.bias, w.scales, w.w_gate, w.w_up, w.w_down, w.dense_gate, w.dense_up,
+            w.dense_down, w.shared_gate, w.shared_up, w.shared_down]
+    for a in keep:
+        if a is not None:
+            assert a.dtype == np.float32 and a.flags["C_CONTIGUOUS"]
+    L = _Layer(d, E, top_k, ff, dff, _p(w.gate), _p(w.bias), _p(w.scales), _p(w.w_gate),
+               _p(w.w_up), _p(w.w_down), _p(w.shared_gate), _p(w.shared_up), _p(w.shared_down),
+               _p(w.dense_gate), _p(w.dense_up), _p(w.dense_down))
+    return L, keep
+
+
+def moe_forward(w, x, top_k: int):
+    """MoELayer::forward (moe.rs:145-177).  Returns out [T,d], idx, w, counts."""
+    x = _f32(x)
+    T, d = x.shape
+    L, _keep = _layer_struct(w, top_k)
+    kk = min(top_k, w.gate.shape[1])
+    out = np.empty((T, d), np.float32)
+    idx = np.empty((T, kk), np.int32)
+    wt = np.empty((T, kk), np.float32)
+    counts = np.zeros(w.gate.shape[1], np.int64)
+    lib().noor_oracle_moe_forward(ctypes.byref(L), _p(x), T, _p(out), _p(idx, _i32p), _p(wt),
+                                  _p(counts, _i64p))
+    return out, idx, wt, counts
+
+
+def parallel_forward(w, x, top_k: int):
+    """ParallelFFN::forward (parallel_ffn.rs:30-36): (dense + moe) / sqrt(2)."""
+    x = _f32(x)
+    T, d = x.shape
+    L, _keep = _layer_struct(w, top_k)
+    kk = min(top_k, w.gate.shape[1])
+    out = np.empty((T, d), np.float32)
+    idx = np.empty((T, kk), np.int32)
+    wt = np.empty((T, kk), np.float32)
+    counts = np.zeros(w.gate.shape[1], np.int64)
+    lib().noor_oracle_parallel_forward(ctypes.byref(L), _p(x), T, _p(out), _p(idx, _i32p), _p(wt),
+                                       _p(counts, _i64p))
+    return out, idx, wt, counts
+
+
+def rms_norm(a, weight, eps: float) -> np.ndarray:
+    a, weight = _f32(a), _f32(weight)
+    out = np.empty_like(a)
+    dim = a.shape[-1]
+    lib().noor_oracle_rms_norm(_p(a), _p(weight), a.size // dim, dim, eps, _p(out))
+    return out
+
+
+def smebu_update(momentum, biases, fractions, kappa: float, beta: float, lam: float):
+    """SMEBU::update (smebu.rs:36-48), in place on momentum and biases."""
+    assert momentum.dtype == np.float32 and biases.dtype == np.float32
+    fr = _f32(fractions)
+    lib().noor_oracle_smebu_update(_p(momentum), _p(biases), _p(fr), momentum.size, kappa, beta, lam)
+
+
+# ------------------------------------------------- independent numpy mirror
+
+def np_parallel_forward(w, x, top_k: int):
+    """Second, vectorised restatement of ParallelFFN::forward in numpy (f64
+    accumulation), used only to cross-check the C oracle within tolerance."""
+    x64 = np.asarray(x, np.float64)
+    g = x64 @ w.gate.astype(np.float64) + w.bias.astype(np.float64)[None, :]
+    s = 1.0 / (1.0 + np.exp(-g))
+    order = np.argsort(-s, axis=1, kind="stable")[:, :top_k]
+    wt = np.take_along_axis(s, order, axis=1) * w.scales.astype(np.float64)[order]
+    T, d = x64.shape
+    moe = np.zeros((T, d))
+    for e in range(w.gate.shape[1]):
+        rows, slot = np.nonzero(order == e)
+        if rows.size == 0:
+            continue
+        xe = x64[rows]
+        gg = xe @ w.w_gate[e].astype(np.float64)
+        uu = xe @ w.w_up[e].astype(np.float64)
+        h = gg / (1.0 + np.exp(-gg)) * uu
+        moe[rows] += wt[rows, slot][:, None] * (h @ w.w_down[e].astype(np.float64))
+    if w.shared_gate is not None:
+        gg = x64 @ w.shared_gate.astype(np.float64)
+        uu = x64 @ w.shared_up.astype(np.float64)
+        moe += (gg / (1.0 + np.exp(-gg)) * uu) @ w.shared_down.astype(np.float64)
+    gg = x64 @ w.dense_gate.astype(np.float64)
+    uu = x64 @ w.dense_up.astype(np.float64)
+    c = np.sqrt(2.0 / np.pi)
+    ge = 0.5 * gg * (1.0 + np.tanh(c * (gg + 0.044715 * gg ** 3)))
+    dense = (ge * uu) @ w.dense_down.astype(np.float64)
+    return (dense + moe) / np.sqrt(2.0), order.astype(np.int32), wt
