@@ -169,6 +169,32 @@ NOOR_MOE_API int noor_moe_profile_end(noor_moe_handle* h, char* names, float* to
 /* Number of kernels this handle has launched since creation. */
 NOOR_MOE_API int64_t noor_moe_launch_count(const noor_moe_handle* h);
 
+/* ---- routing for callers that cannot allocate device memory ---- */
+
+/* Size of the library's fixed routing scratch (one per GPU, held until exit). */
+#define NOOR_MOE_STATIC_SCRATCH_BYTES (2 * 1024 * 1024)
+
+/* No counterpart in the reference: an addition of this library.
+ * The router plus utilization histogram of noor_moe_route, without a handle
+ * and without any device allocation, for callers that cannot call cudaMalloc
+ * (code recording a CUDA graph, where allocation is not allowed during
+ * capture, or hosts that give all device memory to their own pool up front).
+ * All pointers are device pointers; the call is enqueued on `stream`.
+ *   x       [T, d]  f32 (dtype F32) or BF16 bits (dtype BF16)
+ *   gate    F32: [d, E] f32, the reference layout (moe.rs:7);
+ *           BF16: [roundup(E, 8), d] BF16 bits, the gate transposed, rows >= E zero
+ *   bias, scales [E] f32;  outputs idx [T, k] int32, w [T, k] f32, counts [E] int64.
+ * Working memory comes from one fixed array of NOOR_MOE_STATIC_SCRATCH_BYTES
+ * per GPU; a call whose T, E, k would need more returns NOOR_MOE_ERR_INVALID
+ * (BF16 with E = 32, k = 4 fits about 100k tokens; F32 stores the scores too
+ * and fits fewer).  The first call on each device looks up the array's device
+ * address; make that first call before any stream capture.  Every call shares
+ * the array and it keeps the last call's contents, so calls that can overlap
+ * on the GPU (different streams, different host threads) race: serialise them. */
+NOOR_MOE_API int noor_moe_route_static(const void* x, const void* gate, const float* bias, const float* scales,
+                                       int64_t T, int32_t d, int32_t E, int32_t top_k, int32_t dtype,
+                                       int32_t* idx, float* w, int64_t* counts, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -38,7 +38,7 @@ EXPORTED_SYMBOLS = (
     "noor_moe_route", "noor_matmul_f32", "noor_moe_last_error", "noor_moe_sync", "noor_moe_destroy",
     "noor_moe_comm_id_size", "noor_moe_comm_get_id", "noor_moe_comm_init_rank",
     "noor_moe_comm_destroy", "noor_moe_profile_begin", "noor_moe_profile_end",
-    "noor_moe_launch_count", "noor_moe_ep_plan",
+    "noor_moe_launch_count", "noor_moe_ep_plan", "noor_moe_route_static",
 )
 
 
@@ -94,6 +94,8 @@ def lib() -> ctypes.CDLL:
                                        ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
     L.noor_moe_launch_count.argtypes = [_vp]
     L.noor_moe_launch_count.restype = ctypes.c_int64
+    L.noor_moe_route_static.argtypes = [_vp, _vp, _vp, _vp, _i64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                        ctypes.c_int32, _vp, _vp, _vp, _vp]
     _lib = L
     return L
 
@@ -222,6 +224,14 @@ class Handle:
             nm = raw[32 * i:32 * (i + 1)].split(b"\0", 1)[0].decode()
             out[nm] = {"total_ms": float(tot[i]), "launches": int(cnt[i])}
         return out
+
+
+def route_static(x_ptr: int, gate_ptr: int, bias_ptr: int, scales_ptr: int, T: int, d: int, E: int, top_k: int,
+                 dtype: int, idx_ptr: int, w_ptr: int, counts_ptr: int, stream: int) -> None:
+    """noor_moe_route_static: routing with the library's fixed scratch, no
+    handle and no device allocation (device pointers, enqueued on `stream`)."""
+    check(lib().noor_moe_route_static(x_ptr, gate_ptr, bias_ptr, scales_ptr, T, d, E, top_k, dtype, idx_ptr,
+                                      w_ptr, counts_ptr, stream or None))
 
 
 def comm_get_id() -> bytes:

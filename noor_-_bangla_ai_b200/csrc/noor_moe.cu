@@ -24,6 +24,7 @@
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <mutex>
 #include <thread>
 #include <vector>
 
@@ -1099,3 +1100,114 @@ int noor_moe_profile_end(noor_moe_handle* h, char* names, float* total_ms, int32
 int64_t noor_moe_launch_count(const noor_moe_handle* h) { return h ? h->launches : 0; }
 
 }  // extern "C"
+
+// ============================================================== routing without allocation
+//
+// noor_moe_route_static runs the router and the utilization histogram
+// without a handle and without allocating: its working memory (per-pick
+// ranks, per-block histograms and bases, the scan's tables and, for F32
+// layers, the score matrix) lives in the file-scope device array below.  It is
+// for callers that cannot call cudaMalloc: code recording a CUDA graph (an
+// allocation is not allowed while a stream is being captured), and hosts that
+// hand all device memory to their own pool up front and forbid allocation
+// afterwards.  Every GPU that loads this library holds the array until exit.
+
+static __device__ __align__(256) unsigned char g_route_scratch[NOOR_MOE_STATIC_SCRATCH_BYTES];
+
+namespace {
+
+std::mutex g_scratch_mu;
+void* g_scratch_addr[256] = {nullptr};  // device address of g_route_scratch, per CUDA ordinal
+
+// Looks up the array's device address once per device, with that device
+// current.  In host code the name g_route_scratch is only a host-side stand-in,
+// never a usable device address.
+int route_scratch_address(int dev, void** out) {
+  if (dev < 0 || dev >= 256) return fail(NOOR_MOE_ERR_INVALID, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* ptr = nullptr;
+    CK(cudaGetSymbolAddress(&ptr, g_route_scratch));
+    g_scratch_addr[dev] = ptr;
+  }
+  *out = g_scratch_addr[dev];
+  return NOOR_MOE_OK;
+}
+
+size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+}  // namespace
+
+extern "C" int noor_moe_route_static(const void* x, const void* gate, const float* bias, const float* scales,
+                                     int64_t T, int32_t d, int32_t E, int32_t top_k, int32_t dtype,
+                                     int32_t* idx, float* w, int64_t* counts, void* stream) {
+  if (!x || !gate || !bias || !scales || !idx || !w || !counts)
+    return fail(NOOR_MOE_ERR_INVALID, "null argument");
+  if (dtype != NOOR_DTYPE_F32 && dtype != NOOR_DTYPE_BF16) return fail(NOOR_MOE_ERR_INVALID, "unknown dtype");
+  if (T <= 0 || d <= 0 || E <= 0 || top_k <= 0) return fail(NOOR_MOE_ERR_INVALID, "sizes must be positive");
+  const int k = std::min(top_k, E);
+  if (k > router::kMaxTopK) return fail(NOOR_MOE_ERR_UNSUPPORTED, "top_k > %d", router::kMaxTopK);
+  if (dtype == NOOR_DTYPE_BF16 && (E > router::kMaxExpertsTC || d % 64 != 0))
+    return fail(NOOR_MOE_ERR_UNSUPPORTED, "BF16 routing needs E <= %d and d_model a multiple of 64",
+                router::kMaxExpertsTC);
+  if (dtype == NOOR_DTYPE_F32 && E > 256) return fail(NOOR_MOE_ERR_UNSUPPORTED, "at most 256 experts");
+  if (T > INT32_MAX / k) return fail(NOOR_MOE_ERR_INVALID, "too many tokens");
+  const int Epad = (E + 7) / 8 * 8;
+  const int tpb = dtype == NOOR_DTYPE_BF16 ? 64 * (Epad / 8 <= 8 ? 2 : 1) : router::kTopkTPB;
+  const int64_t nblk = (T + tpb - 1) / tpb;
+  // carve the array: ranks | block histograms | block bases | segment starts | tile starts | [scores]
+  const size_t off_lrank = 0;
+  const size_t off_hist = align256(off_lrank + (size_t)T * k * 4);
+  const size_t off_base = align256(off_hist + (size_t)nblk * E * 4);
+  const size_t off_seg = align256(off_base + (size_t)nblk * E * 4);
+  const size_t off_mt = align256(off_seg + (size_t)(E + 1) * 4);
+  const size_t off_scores = align256(off_mt + (size_t)(E + 1) * 4);
+  const size_t need = dtype == NOOR_DTYPE_F32 ? off_scores + (size_t)T * E * 4 : off_scores;
+  if (need > (size_t)NOOR_MOE_STATIC_SCRATCH_BYTES)
+    return fail(NOOR_MOE_ERR_INVALID,
+                "noor_moe_route_static: %lld tokens x %d experts (top-%d) need %zu bytes of scratch, more than "
+                "the fixed %d bytes; split the batch or use noor_moe_route",
+                (long long)T, E, k, need, NOOR_MOE_STATIC_SCRATCH_BYTES);
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  void* base = nullptr;
+  CKR(route_scratch_address(dev, &base));
+  uint8_t* sb = static_cast<uint8_t*>(base);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  router::RouterOut ro{idx, w, reinterpret_cast<int32_t*>(sb + off_lrank), reinterpret_cast<int32_t*>(sb + off_hist)};
+  if (dtype == NOOR_DTYPE_BF16) {
+    const bf16* xg = static_cast<const bf16*>(x);
+    const bf16* gt = static_cast<const bf16*>(gate);
+#define NOOR_STATIC_ROUTE_CASE(NF_, MF_)                                                                  \
+  case NF_:                                                                                               \
+    router::route_bf16_kernel<NF_, MF_><<<(unsigned)nblk, 128, 0, s>>>(xg, gt, bias, scales, (int32_t)T, d, E, k, ro); \
+    break;
+    switch (Epad / 8) {
+      NOOR_STATIC_ROUTE_CASE(1, 2) NOOR_STATIC_ROUTE_CASE(2, 2) NOOR_STATIC_ROUTE_CASE(3, 2)
+      NOOR_STATIC_ROUTE_CASE(4, 2) NOOR_STATIC_ROUTE_CASE(5, 2) NOOR_STATIC_ROUTE_CASE(6, 2)
+      NOOR_STATIC_ROUTE_CASE(7, 2) NOOR_STATIC_ROUTE_CASE(8, 2) NOOR_STATIC_ROUTE_CASE(9, 1)
+      NOOR_STATIC_ROUTE_CASE(10, 1) NOOR_STATIC_ROUTE_CASE(11, 1) NOOR_STATIC_ROUTE_CASE(12, 1)
+      NOOR_STATIC_ROUTE_CASE(13, 1) NOOR_STATIC_ROUTE_CASE(14, 1) NOOR_STATIC_ROUTE_CASE(15, 1)
+      NOOR_STATIC_ROUTE_CASE(16, 1)
+      default:
+        return fail(NOOR_MOE_ERR_UNSUPPORTED, "tensor-core router supports at most 128 experts");
+    }
+#undef NOOR_STATIC_ROUTE_CASE
+  } else {
+    float* scores = reinterpret_cast<float*>(sb + off_scores);
+    const int64_t n = T * E;
+    router::route_f32_scores_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+        static_cast<const float*>(x), static_cast<const float*>(gate), bias, (int32_t)T, d, E, scores);
+    const size_t smem = (size_t)(k * tpb / 32) * E * 4;
+    router::topk_from_scores_kernel<<<(unsigned)nblk, router::kTopkTPB, smem, s>>>(scores, scales, (int32_t)T, E,
+                                                                                    k, ro);
+  }
+  CK(cudaGetLastError());
+  const int C = std::max(1, dispatch::kScanThreads / E);
+  dispatch::scan_segments_kernel<<<1, dispatch::kScanThreads, E * C * 4, s>>>(
+      reinterpret_cast<const int32_t*>(sb + off_hist), (int32_t)nblk, E, tc::BM, counts,
+      reinterpret_cast<int32_t*>(sb + off_seg), reinterpret_cast<int32_t*>(sb + off_base),
+      reinterpret_cast<int32_t*>(sb + off_mt));
+  CK(cudaGetLastError());
+  return NOOR_MOE_OK;
+}
