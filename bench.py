@@ -132,6 +132,9 @@ def cpu_sample_tokens(cfg):
 
 # ------------------------------------------------------------------ reference arm
 
+REFERENCE_BUDGET_S = 150.0  # whole --impl reference run, warm-up included
+
+
 def run_reference(args):
     rank, _, world = env_rank()
     if rank != 0:
@@ -139,13 +142,20 @@ def run_reference(args):
     cfg = W.CONFIGS[args.config]
     T_rank, scaling = layer_tokens(cfg, world)
     w = W.make_weights(cfg)
-    n = cpu_sample_tokens(cfg)
-    x = W.make_tokens(cfg, tokens=n)
     from oracle import oracle as O
     cores = os.cpu_count() or 1
     blas = O.use_openblas(cores)
     times = []
     try:
+        # size each step's sample so that warm-up + K steps fit the budget
+        cal = W.make_tokens(cfg, tokens=64)
+        O.parallel_forward(w, cal[:8], cfg.top_k)
+        t0 = time.perf_counter()
+        O.parallel_forward(w, cal, cfg.top_k)
+        tps = 64 / max(time.perf_counter() - t0, 1e-6)
+        n = int(REFERENCE_BUDGET_S * tps / max(1, args.steps + args.warmup))
+        n = max(16, min(cpu_sample_tokens(cfg), n))
+        x = W.make_tokens(cfg, tokens=n)
         for i in range(args.warmup + args.steps):
             t0 = time.perf_counter()
             O.parallel_forward(w, x, cfg.top_k)
@@ -232,6 +242,27 @@ def run_ours(args):
         step()
     barrier()
 
+    # One GPU: the timed steps replay one captured forward (a CUDA graph);
+    # under expert parallelism the forward waits on the host for the exchange
+    # plan, so the steps are plain calls.
+    graph = None
+    launches_per_step = None
+    if world == 1 and not args.no_graph:
+        cs = torch.cuda.Stream(dev)
+        cs.wait_stream(stream)
+        with torch.cuda.stream(cs):
+            h.forward_device(x_dev.data_ptr(), out_dev.data_ptr(), T, cs.cuda_stream, counts_ptr=counts.data_ptr())
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        l0 = h.launch_count()
+        with torch.cuda.graph(graph, stream=cs):
+            h.forward_device(x_dev.data_ptr(), out_dev.data_ptr(), T, cs.cuda_stream, counts_ptr=counts.data_ptr())
+        launches_per_step = h.launch_count() - l0
+        for _ in range(args.warmup):
+            flush.zero_()
+            graph.replay()
+        barrier()
+
     # ---- timed region: device events around each step, L2 flushed in between
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -239,17 +270,33 @@ def run_ours(args):
     sampler.start()
     time.sleep(0.3)
     launches0 = h.launch_count()
-    h.profile_begin(args.steps * 32)
+    if graph is None:
+        h.profile_begin(args.steps * 16)
     barrier()
     for i in range(args.steps):
         flush.zero_()
         starts[i].record(stream)
-        step()
+        if graph is None:
+            step()
+        else:
+            graph.replay()
         ends[i].record(stream)
     barrier()
-    prof = h.profile_end()
-    launches = h.launch_count() - launches0
     clocks = sampler.stop()
+    if graph is None:
+        prof = h.profile_end()
+        launches = h.launch_count() - launches0
+    else:
+        launches = launches_per_step * args.steps
+        # per-kernel times: the same forward, uncaptured, with an event pair
+        # around each of its kernels
+        prof_steps = min(args.steps, 200)
+        h.profile_begin(prof_steps * 16)
+        for i in range(prof_steps):
+            flush.zero_()
+            step()
+        barrier()
+        prof = h.profile_end()
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     tot_ms = sum(step_ms)
     if world > 1:
@@ -262,7 +309,7 @@ def run_ours(args):
     value = T * world * args.steps / (tot_ms / 1e3)
 
     # ---- end to end through the public API: pinned host in, pinned host out
-    e2e_steps = max(3, min(args.steps, 20))
+    e2e_steps = max(3, min(args.steps, 50))
     for _ in range(2):
         x_dev.copy_(x_host, non_blocking=True)
         step()
@@ -311,6 +358,8 @@ def run_ours(args):
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes,
                     "api": "noor_moe_forward (device mode) with pinned-host H2D/D2H in the timed region"},
             "gpu_launches": launches,
+            "timing": ("CUDA-graph replay of one forward per step; per-kernel times from an uncaptured pass"
+                       if graph is not None else "plain calls; per-kernel events in the timed region"),
             "roofline": roof,
             "kernels": kern,
             "clocks": clocks,
@@ -345,7 +394,8 @@ def kernel_rooflines(cfg, T, world, prof, pk, pk_kind, h, counts):
     hbm = pk.get("hbm_gbs")
     by = W.algorithmic_bytes(cfg, T)
     spec = {
-        "router": ("hbm", by["router"]),
+        "router_scores": ("hbm", by["router_scores"]),
+        "router_topk": ("hbm", by["router_topk"]),
         "permute": ("hbm", by["permute"]),
         "combine": ("hbm", by["combine"]),
         "expert_gemm1": ("tensor", 2.0 * R * d * 2 * ff),
@@ -374,11 +424,12 @@ def kernel_rooflines(cfg, T, world, prof, pk, pk_kind, h, counts):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=1500)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="edge", choices=sorted(W.CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="time plain calls instead of a captured forward")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -172,7 +172,7 @@ NOOR_MOE_API int64_t noor_moe_launch_count(const noor_moe_handle* h);
 /* ---- routing for callers that cannot allocate device memory ---- */
 
 /* Size of the library's fixed routing scratch (one per GPU, held until exit). */
-#define NOOR_MOE_STATIC_SCRATCH_BYTES (2 * 1024 * 1024)
+#define NOOR_MOE_STATIC_SCRATCH_BYTES (8 * 1024 * 1024)
 
 /* No counterpart in the reference: an addition of this library.
  * The router plus utilization histogram of noor_moe_route, without a handle
@@ -186,9 +186,9 @@ NOOR_MOE_API int64_t noor_moe_launch_count(const noor_moe_handle* h);
  *   bias, scales [E] f32;  outputs idx [T, k] int32, w [T, k] f32, counts [E] int64.
  * Working memory comes from one fixed array of NOOR_MOE_STATIC_SCRATCH_BYTES
  * per GPU; a call whose T, E, k would need more returns NOOR_MOE_ERR_INVALID
- * (BF16 with E = 32, k = 4 fits about 100k tokens; F32 stores the scores too
- * and fits fewer).  The first call on each device looks up the array's device
- * address; make that first call before any stream capture.  Every call shares
+ * (E = 32, k = 4: about 450k tokens for BF16, 57k for F32, which also keeps
+ * the f32 scores there).  The first call on each device looks up the array's
+ * device address; make that first call before any stream capture.  Every call shares
  * the array and it keeps the last call's contents, so calls that can overlap
  * on the GPU (different streams, different host threads) race: serialise them. */
 NOOR_MOE_API int noor_moe_route_static(const void* x, const void* gate, const float* bias, const float* scales,

@@ -85,6 +85,12 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 // silu(x) = x / (1 + exp(-x)); gelu(x) = 0.5x(1 + tanh(sqrt(2/pi)(x + 0.044715x^3))).
 __device__ __forceinline__ float act_silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
 
+// SiLU for outputs rounded to BF16 (tensor-core epilogues): the fast
+// exponential and approximate divide are within a few f32 ulp, far below the
+// BF16 rounding (2^-8 relative) that follows.  exp(-x) overflowing to +inf
+// for x < -88 gives x / inf = -0, the limit of silu.
+__device__ __forceinline__ float act_silu_bf16out(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
 __device__ __forceinline__ float act_gelu_tanh(float x) {
   // (2.0f32 / PI).sqrt() evaluated in f32, as the reference does: 0x1.988452p-1
   const float sqrt_2_pi = 0x1.988452p-1f;

@@ -16,14 +16,75 @@ namespace dispatch {
 
 // ------------------------------------------------------------------ scan
 
-// One block.  From the per-token-block histograms hist[nblk][E]:
-//   counts[e]       = picks of expert e (int64, the API's utilization counts)
-//   seg_start[e]    = first row of expert e's segment (exclusive scan), [E+1]
-//   blk_base[b][e]  = first row of block b's picks of expert e
-//   mtile_start[e]  = first BM-row tile of expert e in the grouped GEMM, [E+1]
-// Expert segments are laid out in expert order; under expert parallelism the
-// experts of each rank are contiguous, so the rows bound for each rank are too.
 constexpr int kScanThreads = 1024;
+
+__device__ __forceinline__ int warp_inclusive_scan(int v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += n;
+  }
+  return v;
+}
+
+// From the per-token-block histograms, stored expert-major hist[E][nblk]:
+//   blk_base[e][b]  = first row of block b's picks of expert e
+//   seg_start[e]    = first row of expert e's segment, [E+1]
+//   counts[e]       = picks of expert e (int64, the API's utilization counts)
+//   mtile_start[e]  = first BM-row tile of expert e in the grouped GEMM, [E+1]
+// Because the histograms are expert-major, blk_base is the exclusive prefix
+// sum of the flattened array and seg_start[e] = blk_base[e][0].  Expert
+// segments are laid out in expert order; under expert parallelism the experts
+// of each rank are contiguous, so the rows bound for each rank are too.
+// Runs in one thread block of any multiple of 32 threads (s_warp: 32 ints,
+// s_seg: E+1 ints); hist is read through L2 (ld.cg), so a block may scan
+// histograms that other blocks of the same grid have just written.
+__device__ void scan_segments_block(const int32_t* __restrict__ hist, int32_t nblk, int32_t E, int32_t BM,
+                                    int64_t* __restrict__ counts, int32_t* __restrict__ seg_start,
+                                    int32_t* __restrict__ blk_base, int32_t* __restrict__ mtile_start,
+                                    int32_t* s_warp, int32_t* s_seg) {
+  const int N = E * nblk;
+  const int nt = blockDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = nt >> 5;
+  const int per = (N + nt - 1) / nt;
+  const int i0 = min(N, (int)threadIdx.x * per), i1 = min(N, i0 + per);
+  int sum = 0;
+#pragma unroll 16
+  for (int i = i0; i < i1; ++i) sum += __ldcg(hist + i);
+  const int incl = warp_inclusive_scan(sum);
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int v = lane < nwarps ? s_warp[lane] : 0;
+    const int vi = warp_inclusive_scan(v);
+    if (lane < nwarps) s_warp[lane] = vi - v;
+    if (lane == nwarps - 1) s_seg[E] = vi;  // total picks
+  }
+  __syncthreads();
+  int run = s_warp[warp] + incl - sum;
+#pragma unroll 16
+  for (int i = i0; i < i1; ++i) {
+    const int v = __ldcg(hist + i);
+    blk_base[i] = run;
+    run += v;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += nt) s_seg[e] = blk_base[(int64_t)e * nblk];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int tiles = 0;
+    for (int e = 0; e < E; ++e) {
+      const int c = s_seg[e + 1] - s_seg[e];
+      counts[e] = c;
+      seg_start[e] = s_seg[e];
+      mtile_start[e] = tiles;
+      tiles += (c + BM - 1) / BM;
+    }
+    seg_start[E] = s_seg[E];
+    mtile_start[E] = tiles;
+  }
+}
 
 __global__ void __launch_bounds__(kScanThreads) scan_segments_kernel(const int32_t* __restrict__ hist, int32_t nblk,
                                                                      int32_t E, int32_t BM,
@@ -31,52 +92,9 @@ __global__ void __launch_bounds__(kScanThreads) scan_segments_kernel(const int32
                                                                      int32_t* __restrict__ seg_start,
                                                                      int32_t* __restrict__ blk_base,
                                                                      int32_t* __restrict__ mtile_start) {
-  extern __shared__ int32_t s_part[];  // [E][C]
+  __shared__ int32_t s_warp[32];
   __shared__ int32_t s_seg[1025];
-  const int C = max(1, kScanThreads / E);  // chunks per expert
-  const int chunk = (nblk + C - 1) / C;
-  const int e = threadIdx.x / C;
-  const int c = threadIdx.x - e * C;
-  const bool active = e < E;
-  const int b0 = c * chunk, b1 = min(nblk, b0 + chunk);
-  int sum = 0;
-  if (active)
-    for (int b = b0; b < b1; ++b) sum += hist[(int64_t)b * E + e];
-  if (active) s_part[e * C + c] = sum;
-  __syncthreads();
-  if (threadIdx.x < E) {
-    const int ee = threadIdx.x;
-    int run = 0;
-    for (int cc = 0; cc < C; ++cc) {
-      const int v = s_part[ee * C + cc];
-      s_part[ee * C + cc] = run;
-      run += v;
-    }
-    s_seg[ee] = run;  // total for expert ee (scanned below)
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0, tiles = 0;
-    for (int ee = 0; ee < E; ++ee) {
-      const int v = s_seg[ee];
-      counts[ee] = v;
-      seg_start[ee] = run;
-      mtile_start[ee] = tiles;
-      s_seg[ee] = run;
-      run += v;
-      tiles += (v + BM - 1) / BM;
-    }
-    seg_start[E] = run;
-    mtile_start[E] = tiles;
-  }
-  __syncthreads();
-  if (active) {
-    int run = s_seg[e] + s_part[e * C + c];
-    for (int b = b0; b < b1; ++b) {
-      blk_base[(int64_t)b * E + e] = run;
-      run += hist[(int64_t)b * E + e];
-    }
-  }
+  scan_segments_block(hist, nblk, E, BM, counts, seg_start, blk_base, mtile_start, s_warp, s_seg);
 }
 
 // ------------------------------------------------------------------ permute
@@ -86,19 +104,19 @@ __global__ void __launch_bounds__(kScanThreads) scan_segments_kernel(const int32
 constexpr int kPermuteWarps = 8;
 
 __global__ void __launch_bounds__(kPermuteWarps * 32) permute_rows_kernel(
-    const uint8_t* __restrict__ x, int32_t row_bytes, int32_t T, int32_t k, int32_t E, int32_t tpb,
+    const uint8_t* __restrict__ x, int32_t row_bytes, int32_t T, int32_t k, int32_t nblk, int32_t tpb,
     const int32_t* __restrict__ idx, const int32_t* __restrict__ lrank, const int32_t* __restrict__ blk_base,
     uint8_t* __restrict__ xp, int32_t* __restrict__ dst_row) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int32_t t = blockIdx.x * kPermuteWarps + warp;
   if (t >= T) return;
   int32_t dst[8];
-  const int32_t* bb = blk_base + (int64_t)(t / tpb) * E;
+  const int32_t* bb = blk_base + t / tpb;  // blk_base[e][block] is bb[e * nblk]
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     if (i < k) {
       const int32_t e = __ldg(idx + (int64_t)t * k + i);
-      dst[i] = __ldg(bb + e) + __ldg(lrank + (int64_t)t * k + i);
+      dst[i] = __ldg(bb + (int64_t)e * nblk) + __ldg(lrank + (int64_t)t * k + i);
       if (lane == 0) dst_row[(int64_t)t * k + i] = dst[i];
     }
   }

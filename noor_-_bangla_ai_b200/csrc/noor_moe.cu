@@ -172,17 +172,24 @@ struct noor_moe_handle {
   bool has_shared = false, has_dense = false;
   CUtensorMap tm_w1{}, tm_w2{}, tm_dw1{}, tm_dw2{}, tm_sw1{}, tm_sw2{};
   int bn2 = 256;  // n-tile of GEMMs whose N is d
+  bool pair2 = false;  // tensor-core GEMMs run on SM pairs (cta_group::2, 256-row tiles)
+  int tile_m = 128;    // rows per GEMM tile of the group tables
 
   // workspaces
   int64_t capT = 0;
+  int64_t cap_recv = 0;  // rows the receive-side buffers (xrecv, h, y) hold
   DevBuf x_in, out_buf, idx, wts, lrank, dst_row, blk_hist, blk_base, counts64, counts_glob, seg_start, mtile_start;
   DevBuf scores;
+  DevBuf scan_done;  // zeroed counter for the router's fused scan
   DevBuf xp, h, y, xrecv, ysend;
   DevBuf dense_h, dense_out, shared_h, shared_out;
   DevBuf grp_row, grp_mtile, grp_widx, cnt_recv;
   int64_t* h_cnt = nullptr;  // pinned [E + G*El]
   int32_t* h_grp = nullptr;  // pinned [3 * (G*El + 1)]
   CUtensorMap tm_xp{}, tm_xrecv{}, tm_h{}, tm_xin{}, tm_dh{}, tm_sh{};
+  CUtensorMap tm_user{};            // map of the caller's x (device mode), reused while x and T repeat
+  const void* tm_user_ptr = nullptr;
+  int64_t tm_user_T = -1;
 
   cudaStream_t own = nullptr, aux = nullptr;
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_done = nullptr;
@@ -324,7 +331,7 @@ int ensure_workspace(noor_moe_handle* h, int64_t T) {
   const int64_t b = h->bf16 ? 2 : 4;
   const int64_t Rl = capT * h->k;           // picks made on this rank
   const int64_t Rr = Rl * h->G;             // worst-case rows received under EP
-  const int64_t nblk = (capT + 63) / 64;    // smallest token block is 64
+  const int64_t nblk = (capT + 15) / 16;    // smallest token block: 16 tokens (one router warp)
   const int64_t d = h->d;
   CKR(h->x_in.ensure(capT * d * b));
   CKR(h->out_buf.ensure(capT * d * b));
@@ -342,6 +349,7 @@ int ensure_workspace(noor_moe_handle* h, int64_t T) {
   CKR(h->xp.ensure(Rl * d * b));
   CKR(h->h.ensure(Rr * h->ff * b));
   CKR(h->y.ensure(Rr * d * b));
+  h->cap_recv = std::max(h->cap_recv, Rr);
   if (h->G > 1) {
     CKR(h->xrecv.ensure(Rr * d * b));
     CKR(h->ysend.ensure(Rl * d * b));
@@ -361,8 +369,8 @@ int ensure_workspace(noor_moe_handle* h, int64_t T) {
   }
   if (h->bf16) {
     CKR(encode_kmajor(&h->tm_xp, h->xp.p, Rl, d, tc::BM));
-    if (h->G > 1) CKR(encode_kmajor(&h->tm_xrecv, h->xrecv.p, Rr, d, tc::BM));
-    CKR(encode_kmajor(&h->tm_h, h->h.p, Rr, h->ff, tc::BM));
+    if (h->G > 1) CKR(encode_kmajor(&h->tm_xrecv, h->xrecv.p, h->cap_recv, d, tc::BM));
+    CKR(encode_kmajor(&h->tm_h, h->h.p, h->cap_recv, h->ff, tc::BM));
     CKR(encode_kmajor(&h->tm_xin, h->x_in.p, capT, d, tc::BM));
     if (h->has_dense) CKR(encode_kmajor(&h->tm_dh, h->dense_h.p, capT, h->dff, tc::BM));
     if (h->has_shared) CKR(encode_kmajor(&h->tm_sh, h->shared_h.p, capT, h->ff, tc::BM));
@@ -371,15 +379,72 @@ int ensure_workspace(noor_moe_handle* h, int64_t T) {
   return NOOR_MOE_OK;
 }
 
+// Under expert parallelism the rows a rank receives depend on the other
+// ranks' batches; grow the receive-side buffers to the planned row count.
+int ensure_recv_capacity(noor_moe_handle* h, int64_t rows) {
+  if (rows <= h->cap_recv) return NOOR_MOE_OK;
+  const int64_t cap = round_up(rows, 128);
+  const int64_t b = h->bf16 ? 2 : 4;
+  CKR(h->xrecv.ensure(cap * h->d * b));
+  CKR(h->h.ensure(cap * h->ff * b));
+  CKR(h->y.ensure(cap * h->d * b));
+  h->cap_recv = cap;
+  if (h->bf16) {
+    CKR(encode_kmajor(&h->tm_xrecv, h->xrecv.p, cap, h->d, tc::BM));
+    CKR(encode_kmajor(&h->tm_h, h->h.p, cap, h->ff, tc::BM));
+  }
+  return NOOR_MOE_OK;
+}
+
 // ============================================================== GEMM launchers
+
+// Gather-combine arguments of the dense down projection's fused epilogue.
+struct CombineArgs {
+  const void* y;
+  const int32_t* dst_row;
+  const float* wts;
+  const float* shared;
+  int32_t k;
+};
+
+// Raise a kernel's dynamic shared-memory limit to at least `bytes`.  Up to
+// 48 KB needs no attribute; above it the limit set so far for each
+// (kernel, device) is remembered, so the slow host call runs only when a
+// launch needs more than before.
+template <typename K>
+int ensure_smem_limit(K kern, int bytes) {
+  if (bytes <= 48 * 1024) return NOOR_MOE_OK;
+  static std::mutex mu;
+  struct Entry {
+    const void* kern;
+    int dev;
+    int bytes;
+  };
+  static std::vector<Entry> done;
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  const void* key = reinterpret_cast<const void*>(kern);
+  std::lock_guard<std::mutex> lock(mu);
+  for (auto& e : done)
+    if (e.kern == key && e.dev == dev) {
+      if (e.bytes >= bytes) return NOOR_MOE_OK;
+      CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+      e.bytes = bytes;
+      return NOOR_MOE_OK;
+    }
+  CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.push_back({key, dev, bytes});
+  return NOOR_MOE_OK;
+}
 
 template <int BN, int EPI>
 int launch_tc(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& tA, const CUtensorMap& tB,
-              const GroupTable& gt, int N, int K, void* C, int64_t ldc, int64_t max_mtiles) {
+              const GroupTable& gt, int N, int K, void* C, int64_t ldc, int64_t max_mtiles,
+              const CombineArgs* comb = nullptr) {
   using Cf = tc::Cfg<BN>;
   auto kern = tc::grouped_gemm_kernel<BN, EPI>;
-  CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM_BYTES));
-  tc::Params p;
+  CKR(ensure_smem_limit(kern, Cf::SMEM_BYTES));
+  tc::Params p{};
   p.groups = gt;
   p.N = N;
   p.K = K;
@@ -387,9 +452,59 @@ int launch_tc(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& t
   p.C = C;
   p.ldc = ldc;
   p.err = h->d_err;
+  if (comb) {
+    p.y = static_cast<const bf16*>(comb->y);
+    p.dst_row = comb->dst_row;
+    p.wts = comb->wts;
+    p.shared = comb->shared;
+    p.k = comb->k;
+  }
   const int64_t tiles = std::max<int64_t>(1, max_mtiles * p.n_tiles);
   const int grid = (int)std::min<int64_t>(h->num_sms, tiles);
   return launch(h, s, kind, [&] { kern<<<grid, tc::NUM_THREADS, Cf::SMEM_BYTES, s>>>(tA, tB, p); });
+}
+
+template <int EPI>
+int launch_tc2(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& tA, const CUtensorMap& tB,
+               const GroupTable& gt, int N, int K, void* C, int64_t ldc, int64_t max_tiles,
+               const CombineArgs* comb = nullptr) {
+  auto kern = tc::grouped_gemm_2cta_kernel<EPI>;
+  CKR(ensure_smem_limit(kern, tc::Cfg2::SMEM_BYTES));
+  tc::Params p{};
+  p.groups = gt;
+  p.N = N;
+  p.K = K;
+  p.n_tiles = N / 256;
+  p.C = C;
+  p.ldc = ldc;
+  p.err = h->d_err;
+  if (comb) {
+    p.y = static_cast<const bf16*>(comb->y);
+    p.dst_row = comb->dst_row;
+    p.wts = comb->wts;
+    p.shared = comb->shared;
+    p.k = comb->k;
+  }
+  const int64_t tiles = std::max<int64_t>(1, max_tiles * p.n_tiles);
+  const int clusters = (int)std::min<int64_t>(h->num_sms / 2, tiles);
+  return launch(h, s, kind, [&] { kern<<<2 * clusters, tc::NUM_THREADS, tc::Cfg2::SMEM_BYTES, s>>>(tA, tB, p); });
+}
+
+// A tensor-core GEMM with the layer's tile shape: SM pairs with 256-row
+// tiles when the layer allows it, else one CTA with 128-row tiles and an
+// n-tile of 256 (or 128 when N is not a multiple of 256).  max_tiles counts
+// tiles of h->tile_m rows.
+template <int EPI>
+int launch_gemm(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& tA, const CUtensorMap& tB,
+                const GroupTable& gt, int N, int K, void* C, int64_t ldc, int64_t max_tiles,
+                const CombineArgs* comb = nullptr) {
+  if (h->pair2) return launch_tc2<EPI>(h, s, kind, tA, tB, gt, N, K, C, ldc, max_tiles, comb);
+  if (N % 256 == 0) return launch_tc<256, EPI>(h, s, kind, tA, tB, gt, N, K, C, ldc, max_tiles, comb);
+  if constexpr (tc::epi_gated(EPI)) {
+    return fail(NOOR_MOE_ERR_UNSUPPORTED, "gated GEMM needs N a multiple of 256");
+  } else {
+    return launch_tc<128, EPI>(h, s, kind, tA, tB, gt, N, K, C, ldc, max_tiles, comb);
+  }
 }
 
 template <int EPI>
@@ -421,32 +536,50 @@ GroupTable dense_group(int64_t rows) {
   return g;
 }
 
-// GLU FFN over `rows` rows of A: out = act(A.Wg) * (A.Wu) . Wd.
-// BF16: tensor cores (tA is A's map); F32: CUDA cores.
-int run_glu_ffn(noor_moe_handle* h, cudaStream_t s, int kind1, int kind2, const CUtensorMap* tA, const void* A,
-                int64_t rows, int ffn, int act_silu, const CUtensorMap* tW1, const CUtensorMap* tW2, const CUtensorMap* tH,
-                const float* g32, const float* u32, const float* d32, void* hbuf, float* out) {
-  const GroupTable gt = dense_group(rows);
+// GLU FFN over `rows` rows of A, in two stages: up() writes
+// hbuf = act(A.Wg) * (A.Wu); down() writes hbuf . Wd either as f32 `out` or,
+// with `comb` (BF16 layers), straight into the layer output through the fused
+// gather-combine epilogue.  BF16: tensor cores (tA is A's map); F32: CUDA cores.
+struct GluFfn {
+  int kind1, kind2;
+  const CUtensorMap* tA;
+  const void* A;
+  int64_t rows;
+  int ffn;
+  bool silu;
+  const CUtensorMap *tW1, *tW2, *tH;
+  const float *g32, *u32, *d32;
+  void* hbuf;
+};
+
+int glu_up(noor_moe_handle* h, cudaStream_t s, const GluFfn& f) {
+  const GroupTable gt = dense_group(f.rows);
   const int d = h->d;
   if (h->bf16) {
-    const int64_t mt = (rows + tc::BM - 1) / tc::BM;
-    if (act_silu)
-      CKR((launch_tc<256, tc::EPI_SWIGLU_BF16>(h, s, kind1, *tA, *tW1, gt, 2 * ffn, d, hbuf, ffn, mt)));
-    else
-      CKR((launch_tc<256, tc::EPI_GEGLU_BF16>(h, s, kind1, *tA, *tW1, gt, 2 * ffn, d, hbuf, ffn, mt)));
-    if (h->bn2 == 256)
-      CKR((launch_tc<256, tc::EPI_STORE_F32>(h, s, kind2, *tH, *tW2, gt, d, ffn, out, d, mt)));
-    else
-      CKR((launch_tc<128, tc::EPI_STORE_F32>(h, s, kind2, *tH, *tW2, gt, d, ffn, out, d, mt)));
-  } else {
-    const int64_t mt = (rows + simt::BM - 1) / simt::BM;
-    if (act_silu)
-      CKR((launch_simt<simt::EPI_SWIGLU>(h, s, kind1, gt, (const float*)A, d, g32, u32, 0, ffn, d, (float*)hbuf, ffn, mt)));
-    else
-      CKR((launch_simt<simt::EPI_GEGLU>(h, s, kind1, gt, (const float*)A, d, g32, u32, 0, ffn, d, (float*)hbuf, ffn, mt)));
-    CKR((launch_simt<simt::EPI_STORE>(h, s, kind2, gt, (const float*)hbuf, ffn, d32, nullptr, 0, d, ffn, out, d, mt)));
+    const int64_t mt = (f.rows + h->tile_m - 1) / h->tile_m;
+    if (f.silu)
+      return launch_gemm<tc::EPI_SWIGLU_BF16>(h, s, f.kind1, *f.tA, *f.tW1, gt, 2 * f.ffn, d, f.hbuf, f.ffn, mt);
+    return launch_gemm<tc::EPI_GEGLU_BF16>(h, s, f.kind1, *f.tA, *f.tW1, gt, 2 * f.ffn, d, f.hbuf, f.ffn, mt);
   }
-  return NOOR_MOE_OK;
+  const int64_t mt = (f.rows + simt::BM - 1) / simt::BM;
+  if (f.silu)
+    return launch_simt<simt::EPI_SWIGLU>(h, s, f.kind1, gt, (const float*)f.A, d, f.g32, f.u32, 0, f.ffn, d,
+                                         (float*)f.hbuf, f.ffn, mt);
+  return launch_simt<simt::EPI_GEGLU>(h, s, f.kind1, gt, (const float*)f.A, d, f.g32, f.u32, 0, f.ffn, d,
+                                      (float*)f.hbuf, f.ffn, mt);
+}
+
+int glu_down(noor_moe_handle* h, cudaStream_t s, const GluFfn& f, void* out, const CombineArgs* comb) {
+  const GroupTable gt = dense_group(f.rows);
+  const int d = h->d;
+  if (h->bf16) {
+    const int64_t mt = (f.rows + h->tile_m - 1) / h->tile_m;
+    if (comb) return launch_gemm<tc::EPI_COMBINE_BF16>(h, s, f.kind2, *f.tH, *f.tW2, gt, d, f.ffn, out, d, mt, comb);
+    return launch_gemm<tc::EPI_STORE_F32>(h, s, f.kind2, *f.tH, *f.tW2, gt, d, f.ffn, out, d, mt);
+  }
+  const int64_t mt = (f.rows + simt::BM - 1) / simt::BM;
+  return launch_simt<simt::EPI_STORE>(h, s, f.kind2, gt, (const float*)f.hbuf, f.ffn, f.d32, nullptr, 0, d, f.ffn,
+                                      (float*)out, d, mt);
 }
 
 // ============================================================== router
@@ -457,36 +590,37 @@ int run_router(noor_moe_handle* h, cudaStream_t s, const void* x, int64_t T, int
   router::RouterOut ro{h->idx.as<int32_t>(), h->wts.as<float>(), h->lrank.as<int32_t>(), h->blk_hist.as<int32_t>()};
   const int E = h->E, k = h->k, d = h->d;
   int tpb = 0;
+  router::FusedScan fs{h->scan_done.as<int>(), h->counts64.as<int64_t>(), h->seg_start.as<int32_t>(),
+                       h->blk_base.as<int32_t>(), h->mtile_start.as<int32_t>(), h->tile_m};
   if (h->bf16) {
     const int NF = h->Epad / 8;
-    const int MF = NF <= 8 ? 2 : 1;
-    tpb = 64 * MF;
+    const int warps = router::route_warps(T, h->num_sms);
+    tpb = 16 * warps;
     const int nblk = (int)((T + tpb - 1) / tpb);
+    const int kc_len = router::route_chunk(d, NF);
+    if (kc_len == 0) return fail(NOOR_MOE_ERR_UNSUPPORTED, "router gate slice does not fit shared memory");
+    const int smem = NF * 8 * (kc_len + 32) * 2;
     const bf16* xg = reinterpret_cast<const bf16*>(x);
     const bf16* gt = h->gate.as<bf16>();
     const float* b = h->bias.as<float>();
     const float* sc = h->scales.as<float>();
-#define NOOR_ROUTE_CASE(NF_, MF_)                                                                          \
-  case NF_:                                                                                                \
-    CKR(launch(h, s, K_ROUTER, [&] {                                                                       \
-      router::route_bf16_kernel<NF_, MF_><<<nblk, 128, 0, s>>>(xg, gt, b, sc, (int32_t)T, d, E, k, ro);    \
-    }));                                                                                                   \
+#define NOOR_ROUTE_CASE(NF_)                                                                                 \
+  case NF_:                                                                                                  \
+    CKR(ensure_smem_limit(router::route_bf16_kernel<NF_>, smem));                                            \
+    CKR(launch(h, s, K_ROUTER, [&] {                                                                         \
+      router::route_bf16_kernel<NF_><<<nblk, 32 * warps, smem, s>>>(xg, gt, b, sc, (int32_t)T, d, E, k, kc_len, ro, \
+                                                                    fs);                                     \
+    }));                                                                                                     \
     break;
     switch (NF) {
-      NOOR_ROUTE_CASE(1, 2) NOOR_ROUTE_CASE(2, 2) NOOR_ROUTE_CASE(3, 2) NOOR_ROUTE_CASE(4, 2)
-      NOOR_ROUTE_CASE(5, 2) NOOR_ROUTE_CASE(6, 2) NOOR_ROUTE_CASE(7, 2) NOOR_ROUTE_CASE(8, 2)
-      NOOR_ROUTE_CASE(9, 1) NOOR_ROUTE_CASE(10, 1) NOOR_ROUTE_CASE(11, 1) NOOR_ROUTE_CASE(12, 1)
-      NOOR_ROUTE_CASE(13, 1) NOOR_ROUTE_CASE(14, 1) NOOR_ROUTE_CASE(15, 1) NOOR_ROUTE_CASE(16, 1)
+      NOOR_ROUTE_CASE(1) NOOR_ROUTE_CASE(2) NOOR_ROUTE_CASE(3) NOOR_ROUTE_CASE(4) NOOR_ROUTE_CASE(5)
+      NOOR_ROUTE_CASE(6) NOOR_ROUTE_CASE(7) NOOR_ROUTE_CASE(8) NOOR_ROUTE_CASE(9) NOOR_ROUTE_CASE(10)
+      NOOR_ROUTE_CASE(11) NOOR_ROUTE_CASE(12) NOOR_ROUTE_CASE(13) NOOR_ROUTE_CASE(14) NOOR_ROUTE_CASE(15)
+      NOOR_ROUTE_CASE(16)
       default:
         return fail(NOOR_MOE_ERR_UNSUPPORTED, "tensor-core router supports at most 128 experts");
     }
 #undef NOOR_ROUTE_CASE
-    CKR(launch(h, s, K_SCAN, [&] {
-      const int C = std::max(1, dispatch::kScanThreads / E);
-      dispatch::scan_segments_kernel<<<1, dispatch::kScanThreads, E * C * 4, s>>>(
-          h->blk_hist.as<int32_t>(), nblk, E, tc::BM, h->counts64.as<int64_t>(), h->seg_start.as<int32_t>(),
-          h->blk_base.as<int32_t>(), h->mtile_start.as<int32_t>());
-    }));
   } else {
     tpb = router::kTopkTPB;
     const int nblk = (int)((T + tpb - 1) / tpb);
@@ -495,16 +629,12 @@ int run_router(noor_moe_handle* h, cudaStream_t s, const void* x, int64_t T, int
       router::route_f32_scores_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
           (const float*)x, h->gate.as<float>(), h->bias.as<float>(), (int32_t)T, d, E, h->scores.as<float>());
     }));
-    const size_t smem = (size_t)(k * tpb / 32) * E * 4;
+    const size_t smem = router::topk_smem_bytes(E, k);
+    CKR(ensure_smem_limit(router::topk_from_scores_kernel, (int)smem));
     CKR(launch(h, s, K_ROUTER_TOPK, [&] {
-      router::topk_from_scores_kernel<<<nblk, router::kTopkTPB, smem, s>>>(h->scores.as<float>(), h->scales.as<float>(),
-                                                                           (int32_t)T, E, k, ro);
-    }));
-    CKR(launch(h, s, K_SCAN, [&] {
-      const int C = std::max(1, dispatch::kScanThreads / E);
-      dispatch::scan_segments_kernel<<<1, dispatch::kScanThreads, E * C * 4, s>>>(
-          h->blk_hist.as<int32_t>(), nblk, E, simt::BM, h->counts64.as<int64_t>(), h->seg_start.as<int32_t>(),
-          h->blk_base.as<int32_t>(), h->mtile_start.as<int32_t>());
+      router::topk_from_scores_kernel<<<nblk, router::kTopkTPB, smem, s>>>(h->scores.as<float>(),
+                                                                           h->scales.as<float>(), (int32_t)T, E, k, ro,
+                                                                           fs);
     }));
   }
   *tpb_out = tpb;
@@ -547,11 +677,11 @@ int ep_plan(noor_moe_handle* h, cudaStream_t s, EpPlan& plan) {
   int32_t* row = h->h_grp;
   int32_t* mt = h->h_grp + (ng + 1);
   int32_t* wi = h->h_grp + 2 * (ng + 1);
-  const int BM = h->bf16 ? tc::BM : simt::BM;
-  CKR(noor_moe_ep_plan(h->h_cnt, h->h_cnt + E, E, G, BM, plan.send_rows.data(), plan.send_off.data(),
+  CKR(noor_moe_ep_plan(h->h_cnt, h->h_cnt + E, E, G, h->tile_m, plan.send_rows.data(), plan.send_off.data(),
                        plan.recv_rows.data(), plan.recv_off.data(), row, mt, wi));
   plan.recv_total = row[ng];
   plan.mtiles = mt[ng];
+  CKR(ensure_recv_capacity(h, plan.recv_total));
   CK(cudaMemcpyAsync(h->grp_row.p, row, (ng + 1) * 4, cudaMemcpyHostToDevice, s));
   CK(cudaMemcpyAsync(h->grp_mtile.p, mt, (ng + 1) * 4, cudaMemcpyHostToDevice, s));
   CK(cudaMemcpyAsync(h->grp_widx.p, wi, (ng + 1) * 4, cudaMemcpyHostToDevice, s));
@@ -584,25 +714,40 @@ int ep_exchange(noor_moe_handle* h, cudaStream_t s, int kind, const EpPlan& plan
 // ============================================================== forward
 
 // x, out: device pointers of the layer dtype.  tmx: tensor map of x (BF16).
+//
+// One GPU: a single stream, in dependency order.  Expert parallel: the dense
+// (and shared) up projections run on a second stream while the rows cross
+// NVLink; the dense down projection waits for the returned expert rows.
 int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtensorMap* tmx, void* out, int64_t T) {
   const int d = h->d, k = h->k, E = h->E;
   const int64_t b = h->bf16 ? 2 : 4;
+  const GluFfn dense{K_DENSE_GEMM1, K_DENSE_GEMM2, tmx, x, T, h->dff, h->desc.dense_act == NOOR_ACT_SILU,
+                     &h->tm_dw1, &h->tm_dw2, &h->tm_dh, h->dg32.as<float>(), h->du32.as<float>(),
+                     h->dd32.as<float>(), h->dense_h.p};
+  const GluFfn shared{K_SHARED_GEMM1, K_SHARED_GEMM2, tmx, x, T, h->ff, true, &h->tm_sw1, &h->tm_sw2, &h->tm_sh,
+                      h->sg32.as<float>(), h->su32.as<float>(), h->sd32.as<float>(), h->shared_h.p};
+  const bool fuse_combine = h->bf16 && h->has_dense;
+  const bool side = h->G > 1 && (h->has_dense || h->has_shared) && T > 0;
+  cudaStream_t ss = side ? h->aux : s;  // stream of the side branches' up projections
 
-  // Dense / shared branches depend only on x: fork them onto the aux stream.
-  const bool side = (h->has_dense || h->has_shared) && T > 0;
   if (side) {
     CK(cudaEventRecord(h->ev_fork, s));
     CK(cudaStreamWaitEvent(h->aux, h->ev_fork, 0));
-    if (h->has_dense)
-      CKR(run_glu_ffn(h, h->aux, K_DENSE_GEMM1, K_DENSE_GEMM2, tmx, x, T, h->dff, h->desc.dense_act == NOOR_ACT_SILU,
-                      &h->tm_dw1, &h->tm_dw2, &h->tm_dh, h->dg32.as<float>(), h->du32.as<float>(), h->dd32.as<float>(),
-                      h->dense_h.p, h->dense_out.as<float>()));
-    if (h->has_shared)
-      CKR(run_glu_ffn(h, h->aux, K_SHARED_GEMM1, K_SHARED_GEMM2, tmx, x, T, h->ff, 1, &h->tm_sw1, &h->tm_sw2,
-                      &h->tm_sh, h->sg32.as<float>(), h->su32.as<float>(), h->sd32.as<float>(), h->shared_h.p,
-                      h->shared_out.as<float>()));
-    CK(cudaEventRecord(h->ev_join, h->aux));
   }
+  auto side_branches = [&]() -> int {
+    if (T == 0) return NOOR_MOE_OK;
+    if (h->has_dense) {
+      CKR(glu_up(h, ss, dense));
+      if (!fuse_combine) CKR(glu_down(h, ss, dense, h->dense_out.p, nullptr));
+    }
+    if (h->has_shared) {
+      CKR(glu_up(h, ss, shared));
+      CKR(glu_down(h, ss, shared, h->shared_out.p, nullptr));
+    }
+    if (side) CK(cudaEventRecord(h->ev_join, h->aux));
+    return NOOR_MOE_OK;
+  };
+  if (side) CKR(side_branches());
 
   int tpb = 0;
   if (T == 0) {
@@ -610,13 +755,14 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
     CK(cudaMemsetAsync(h->counts64.p, 0, E * 8, s));
   } else {
     CKR(run_router(h, s, x, T, &tpb));
+    CKR(launch(h, s, K_PERMUTE, [&] {
+      const unsigned grid = (unsigned)((T + dispatch::kPermuteWarps - 1) / dispatch::kPermuteWarps);
+      dispatch::permute_rows_kernel<<<grid, dispatch::kPermuteWarps * 32, 0, s>>>(
+          static_cast<const uint8_t*>(x), (int32_t)(d * b), (int32_t)T, k, (int32_t)((T + tpb - 1) / tpb), tpb,
+          h->idx.as<int32_t>(),
+          h->lrank.as<int32_t>(), h->blk_base.as<int32_t>(), h->xp.as<uint8_t>(), h->dst_row.as<int32_t>());
+    }));
   }
-  if (T > 0) CKR(launch(h, s, K_PERMUTE, [&] {
-    const unsigned grid = (unsigned)((T + dispatch::kPermuteWarps - 1) / dispatch::kPermuteWarps);
-    dispatch::permute_rows_kernel<<<grid, dispatch::kPermuteWarps * 32, 0, s>>>(
-        static_cast<const uint8_t*>(x), (int32_t)(d * b), (int32_t)T, k, E, tpb, h->idx.as<int32_t>(),
-        h->lrank.as<int32_t>(), h->blk_base.as<int32_t>(), h->xp.as<uint8_t>(), h->dst_row.as<int32_t>());
-  }));
 
   GroupTable gt;
   const CUtensorMap* tA = &h->tm_xp;
@@ -630,8 +776,7 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
     gt.weight_idx = nullptr;
     gt.G = E;
     gt.dense_rows = -1;
-    const int BM = h->bf16 ? tc::BM : simt::BM;
-    max_mtiles = (T * k + BM - 1) / BM + E;
+    max_mtiles = (T * k + h->tile_m - 1) / h->tile_m + E;
   } else {
     CKR(ep_plan(h, s, plan));
     CKR(ep_exchange(h, s, K_A2A_DISPATCH, plan, h->xp.p, h->xrecv.p, false));
@@ -646,16 +791,13 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
     ybuf = h->ysend.p;
   }
 
+  if (T > 0 && h->G == 1) max_mtiles = std::max<int64_t>(max_mtiles, 1);
   if (max_mtiles > 0) {
     if (h->bf16) {
-      CKR((launch_tc<256, tc::EPI_SWIGLU_BF16>(h, s, K_EXPERT_GEMM1, *tA, h->tm_w1, gt, 2 * h->ff, d, h->h.p, h->ff,
-                                               max_mtiles)));
-      if (h->bn2 == 256)
-        CKR((launch_tc<256, tc::EPI_STORE_BF16>(h, s, K_EXPERT_GEMM2, h->tm_h, h->tm_w2, gt, d, h->ff, h->y.p, d,
-                                                max_mtiles)));
-      else
-        CKR((launch_tc<128, tc::EPI_STORE_BF16>(h, s, K_EXPERT_GEMM2, h->tm_h, h->tm_w2, gt, d, h->ff, h->y.p, d,
-                                                max_mtiles)));
+      CKR(launch_gemm<tc::EPI_SWIGLU_BF16>(h, s, K_EXPERT_GEMM1, *tA, h->tm_w1, gt, 2 * h->ff, d, h->h.p, h->ff,
+                                           max_mtiles));
+      CKR(launch_gemm<tc::EPI_STORE_BF16>(h, s, K_EXPERT_GEMM2, h->tm_h, h->tm_w2, gt, d, h->ff, h->y.p, d,
+                                          max_mtiles));
     } else {
       const int64_t ffd = (int64_t)d * h->ff;
       CKR((launch_simt<simt::EPI_SWIGLU>(h, s, K_EXPERT_GEMM1, gt, (const float*)A32, d, h->wg32.as<float>(),
@@ -667,20 +809,25 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
   if (h->G > 1) CKR(ep_exchange(h, s, K_A2A_COMBINE, plan, h->y.p, h->ysend.p, true));
 
   if (side) CK(cudaStreamWaitEvent(s, h->ev_join, 0));
-  if (T > 0) CKR(launch(h, s, K_COMBINE, [&] {
+  else CKR(side_branches());
+  if (T == 0) return NOOR_MOE_OK;
+  const float* shared_out = h->has_shared ? h->shared_out.as<float>() : nullptr;
+  if (fuse_combine) {
+    const CombineArgs comb{ybuf, h->dst_row.as<int32_t>(), h->wts.as<float>(), shared_out, k};
+    return glu_down(h, s, dense, out, &comb);
+  }
+  return launch(h, s, K_COMBINE, [&] {
     const unsigned grid = (unsigned)((T + dispatch::kCombineWarps - 1) / dispatch::kCombineWarps);
-    const float* dense = h->has_dense ? h->dense_out.as<float>() : nullptr;
-    const float* shared = h->has_shared ? h->shared_out.as<float>() : nullptr;
+    const float* dense_out = h->has_dense ? h->dense_out.as<float>() : nullptr;
     if (h->bf16)
       dispatch::combine_kernel<bf16, bf16><<<grid, dispatch::kCombineWarps * 32, 0, s>>>(
-          (const bf16*)ybuf, h->dst_row.as<int32_t>(), h->wts.as<float>(), dense, shared, (int32_t)T, d, k,
+          (const bf16*)ybuf, h->dst_row.as<int32_t>(), h->wts.as<float>(), dense_out, shared_out, (int32_t)T, d, k,
           (bf16*)out);
     else
       dispatch::combine_kernel<float, float><<<grid, dispatch::kCombineWarps * 32, 0, s>>>(
-          (const float*)ybuf, h->dst_row.as<int32_t>(), h->wts.as<float>(), dense, shared, (int32_t)T, d, k,
+          (const float*)ybuf, h->dst_row.as<int32_t>(), h->wts.as<float>(), dense_out, shared_out, (int32_t)T, d, k,
           (float*)out);
-  }));
-  return NOOR_MOE_OK;
+  });
 }
 
 int global_counts(noor_moe_handle* h, cudaStream_t s, const int64_t** src) {
@@ -758,6 +905,8 @@ int noor_moe_create(const noor_moe_desc* desc, void* nccl_comm, noor_moe_handle*
   h->has_shared = desc->has_shared != 0;
   h->Epad = (h->E + 7) / 8 * 8;
   h->bn2 = (h->d % 256 == 0) ? 256 : 128;
+  h->pair2 = h->bf16 && h->d % 256 == 0;
+  h->tile_m = h->pair2 ? tc::BM2 : (h->bf16 ? tc::BM : simt::BM);
   auto bail = [&](int rc) {
     noor_moe_destroy(h);
     return rc;
@@ -775,6 +924,8 @@ int noor_moe_create(const noor_moe_desc* desc, void* nccl_comm, noor_moe_handle*
         cudaMallocHost(&h->h_grp, 3 * (ng + 1) * 4) != cudaSuccess)
       return bail(fail(NOOR_MOE_ERR_OOM, "pinned host buffers"));
   }
+  if (h->scan_done.ensure(sizeof(int)) != NOOR_MOE_OK || cudaMemset(h->scan_done.p, 0, sizeof(int)) != cudaSuccess)
+    return bail(fail(NOOR_MOE_ERR_CUDA, "scan counter setup failed"));
   const int rc = ensure_workspace(h, std::max<int64_t>(desc->max_tokens, 128));
   if (rc != NOOR_MOE_OK) return bail(rc);
   *out = h;
@@ -859,16 +1010,17 @@ int noor_moe_load_weights(noor_moe_handle* h, const float* gate, const float* bi
     CKR(pack(w_up[h->e0 + le], d, ff, w1, 128, 256, 128));
     CKR(pack(w_down[h->e0 + le], ff, d, h->w2.as<bf16>() + (int64_t)le * d * ff, d, d, 0));
   }
-  CKR(encode_kmajor(&h->tm_w1, h->w1.p, (int64_t)El * 2 * ff, d, 256));
-  CKR(encode_kmajor(&h->tm_w2, h->w2.p, (int64_t)El * d, ff, h->bn2));
+  const int bbox1 = h->pair2 ? 128 : 256, bbox2 = h->pair2 ? 128 : h->bn2;  // rows of B one CTA loads
+  CKR(encode_kmajor(&h->tm_w1, h->w1.p, (int64_t)El * 2 * ff, d, bbox1));
+  CKR(encode_kmajor(&h->tm_w2, h->w2.p, (int64_t)El * d, ff, bbox2));
   if (h->has_dense) {
     CKR(h->dw1.ensure((int64_t)2 * dff * d * 2));
     CKR(h->dw2.ensure((int64_t)d * dff * 2));
     CKR(pack(dense[0], d, dff, h->dw1.as<bf16>(), 128, 256, 0));
     CKR(pack(dense[1], d, dff, h->dw1.as<bf16>(), 128, 256, 128));
     CKR(pack(dense[2], dff, d, h->dw2.as<bf16>(), d, d, 0));
-    CKR(encode_kmajor(&h->tm_dw1, h->dw1.p, 2 * dff, d, 256));
-    CKR(encode_kmajor(&h->tm_dw2, h->dw2.p, d, dff, h->bn2));
+    CKR(encode_kmajor(&h->tm_dw1, h->dw1.p, 2 * dff, d, bbox1));
+    CKR(encode_kmajor(&h->tm_dw2, h->dw2.p, d, dff, bbox2));
   }
   if (h->has_shared) {
     CKR(h->sw1.ensure((int64_t)2 * ff * d * 2));
@@ -876,8 +1028,8 @@ int noor_moe_load_weights(noor_moe_handle* h, const float* gate, const float* bi
     CKR(pack(shared[0], d, ff, h->sw1.as<bf16>(), 128, 256, 0));
     CKR(pack(shared[1], d, ff, h->sw1.as<bf16>(), 128, 256, 128));
     CKR(pack(shared[2], ff, d, h->sw2.as<bf16>(), d, d, 0));
-    CKR(encode_kmajor(&h->tm_sw1, h->sw1.p, 2 * ff, d, 256));
-    CKR(encode_kmajor(&h->tm_sw2, h->sw2.p, d, ff, h->bn2));
+    CKR(encode_kmajor(&h->tm_sw1, h->sw1.p, 2 * ff, d, bbox1));
+    CKR(encode_kmajor(&h->tm_sw2, h->sw2.p, d, ff, bbox2));
   }
   stage.release();
   h->weights = true;
@@ -916,13 +1068,16 @@ static int forward_impl(noor_moe_handle* h, const void* x, void* out, int64_t T,
   }
   const void* xd = x;
   const CUtensorMap* tmx = &h->tm_xin;
-  CUtensorMap tm_user;
   if (host) {
     if (T > 0) CK(cudaMemcpyAsync(h->x_in.p, x, xbytes, cudaMemcpyHostToDevice, s));
     xd = h->x_in.p;
   } else if (h->bf16 && !route_only && (h->has_dense || h->has_shared)) {
-    CKR(encode_kmajor(&tm_user, x, T, h->d, tc::BM));
-    tmx = &tm_user;
+    if (x != h->tm_user_ptr || T != h->tm_user_T) {
+      CKR(encode_kmajor(&h->tm_user, x, T, h->d, tc::BM));
+      h->tm_user_ptr = x;
+      h->tm_user_T = T;
+    }
+    tmx = &h->tm_user;
   }
   if (route_only) {
     int tpb = 0;
@@ -979,7 +1134,7 @@ void noor_moe_destroy(noor_moe_handle* h) {
                       &h->x_in, &h->out_buf, &h->idx, &h->wts, &h->lrank, &h->dst_row, &h->blk_hist,
                       &h->blk_base, &h->counts64, &h->counts_glob, &h->seg_start, &h->mtile_start, &h->scores,
                       &h->xp, &h->h, &h->y, &h->xrecv, &h->ysend, &h->dense_h, &h->dense_out, &h->shared_h,
-                      &h->shared_out, &h->grp_row, &h->grp_mtile, &h->grp_widx, &h->cnt_recv};
+                      &h->shared_out, &h->grp_row, &h->grp_mtile, &h->grp_widx, &h->cnt_recv, &h->scan_done};
     for (DevBuf* b : bufs) b->release();
     if (h->h_cnt) cudaFreeHost(h->h_cnt);
     if (h->h_grp) cudaFreeHost(h->h_grp);
@@ -1147,13 +1302,20 @@ extern "C" int noor_moe_route_static(const void* x, const void* gate, const floa
   if (T <= 0 || d <= 0 || E <= 0 || top_k <= 0) return fail(NOOR_MOE_ERR_INVALID, "sizes must be positive");
   const int k = std::min(top_k, E);
   if (k > router::kMaxTopK) return fail(NOOR_MOE_ERR_UNSUPPORTED, "top_k > %d", router::kMaxTopK);
-  if (dtype == NOOR_DTYPE_BF16 && (E > router::kMaxExpertsTC || d % 64 != 0))
-    return fail(NOOR_MOE_ERR_UNSUPPORTED, "BF16 routing needs E <= %d and d_model a multiple of 64",
+  if (dtype == NOOR_DTYPE_BF16 && (E > router::kMaxExpertsTC || d % 128 != 0))
+    return fail(NOOR_MOE_ERR_UNSUPPORTED, "BF16 routing needs E <= %d and d_model a multiple of 128",
                 router::kMaxExpertsTC);
   if (dtype == NOOR_DTYPE_F32 && E > 256) return fail(NOOR_MOE_ERR_UNSUPPORTED, "at most 256 experts");
   if (T > INT32_MAX / k) return fail(NOOR_MOE_ERR_INVALID, "too many tokens");
   const int Epad = (E + 7) / 8 * 8;
-  const int tpb = dtype == NOOR_DTYPE_BF16 ? 64 * (Epad / 8 <= 8 ? 2 : 1) : router::kTopkTPB;
+  int nsm = 148;
+  {
+    int dev0 = 0;
+    CK(cudaGetDevice(&dev0));
+    CK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev0));
+  }
+  const int warps = router::route_warps(T, nsm);
+  const int tpb = dtype == NOOR_DTYPE_BF16 ? 16 * warps : router::kTopkTPB;
   const int64_t nblk = (T + tpb - 1) / tpb;
   // carve the array: ranks | block histograms | block bases | segment starts | tile starts | [scores]
   const size_t off_lrank = 0;
@@ -1162,7 +1324,7 @@ extern "C" int noor_moe_route_static(const void* x, const void* gate, const floa
   const size_t off_seg = align256(off_base + (size_t)nblk * E * 4);
   const size_t off_mt = align256(off_seg + (size_t)(E + 1) * 4);
   const size_t off_scores = align256(off_mt + (size_t)(E + 1) * 4);
-  const size_t need = dtype == NOOR_DTYPE_F32 ? off_scores + (size_t)T * E * 4 : off_scores;
+  const size_t need = off_scores + (dtype == NOOR_DTYPE_F32 ? (size_t)T * E * 4 : 0);
   if (need > (size_t)NOOR_MOE_STATIC_SCRATCH_BYTES)
     return fail(NOOR_MOE_ERR_INVALID,
                 "noor_moe_route_static: %lld tokens x %d experts (top-%d) need %zu bytes of scratch, more than "
@@ -1175,36 +1337,45 @@ extern "C" int noor_moe_route_static(const void* x, const void* gate, const floa
   uint8_t* sb = static_cast<uint8_t*>(base);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   router::RouterOut ro{idx, w, reinterpret_cast<int32_t*>(sb + off_lrank), reinterpret_cast<int32_t*>(sb + off_hist)};
+  float* scores = reinterpret_cast<float*>(sb + off_scores);
+  const router::FusedScan nofs{nullptr, nullptr, nullptr, nullptr, nullptr, tc::BM};
   if (dtype == NOOR_DTYPE_BF16) {
+    // the same kernel as noor_moe_route, so the results are identical
     const bf16* xg = static_cast<const bf16*>(x);
     const bf16* gt = static_cast<const bf16*>(gate);
-#define NOOR_STATIC_ROUTE_CASE(NF_, MF_)                                                                  \
-  case NF_:                                                                                               \
-    router::route_bf16_kernel<NF_, MF_><<<(unsigned)nblk, 128, 0, s>>>(xg, gt, bias, scales, (int32_t)T, d, E, k, ro); \
+    const int NF = Epad / 8;
+    const int kc_len = router::route_chunk(d, NF);
+    if (kc_len == 0) return fail(NOOR_MOE_ERR_UNSUPPORTED, "router gate slice does not fit shared memory");
+    const int smem = NF * 8 * (kc_len + 32) * 2;
+#define NOOR_STATIC_ROUTE_CASE(NF_)                                                                            \
+  case NF_:                                                                                                    \
+    if (smem > 48 * 1024)                                                                                      \
+      CK(cudaFuncSetAttribute(router::route_bf16_kernel<NF_>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)); \
+    router::route_bf16_kernel<NF_><<<(unsigned)nblk, 32 * warps, smem, s>>>(xg, gt, bias, scales, (int32_t)T, d, E, \
+                                                                            k, kc_len, ro, nofs);                \
     break;
-    switch (Epad / 8) {
-      NOOR_STATIC_ROUTE_CASE(1, 2) NOOR_STATIC_ROUTE_CASE(2, 2) NOOR_STATIC_ROUTE_CASE(3, 2)
-      NOOR_STATIC_ROUTE_CASE(4, 2) NOOR_STATIC_ROUTE_CASE(5, 2) NOOR_STATIC_ROUTE_CASE(6, 2)
-      NOOR_STATIC_ROUTE_CASE(7, 2) NOOR_STATIC_ROUTE_CASE(8, 2) NOOR_STATIC_ROUTE_CASE(9, 1)
-      NOOR_STATIC_ROUTE_CASE(10, 1) NOOR_STATIC_ROUTE_CASE(11, 1) NOOR_STATIC_ROUTE_CASE(12, 1)
-      NOOR_STATIC_ROUTE_CASE(13, 1) NOOR_STATIC_ROUTE_CASE(14, 1) NOOR_STATIC_ROUTE_CASE(15, 1)
-      NOOR_STATIC_ROUTE_CASE(16, 1)
+    switch (NF) {
+      NOOR_STATIC_ROUTE_CASE(1) NOOR_STATIC_ROUTE_CASE(2) NOOR_STATIC_ROUTE_CASE(3) NOOR_STATIC_ROUTE_CASE(4)
+      NOOR_STATIC_ROUTE_CASE(5) NOOR_STATIC_ROUTE_CASE(6) NOOR_STATIC_ROUTE_CASE(7) NOOR_STATIC_ROUTE_CASE(8)
+      NOOR_STATIC_ROUTE_CASE(9) NOOR_STATIC_ROUTE_CASE(10) NOOR_STATIC_ROUTE_CASE(11) NOOR_STATIC_ROUTE_CASE(12)
+      NOOR_STATIC_ROUTE_CASE(13) NOOR_STATIC_ROUTE_CASE(14) NOOR_STATIC_ROUTE_CASE(15) NOOR_STATIC_ROUTE_CASE(16)
       default:
         return fail(NOOR_MOE_ERR_UNSUPPORTED, "tensor-core router supports at most 128 experts");
     }
 #undef NOOR_STATIC_ROUTE_CASE
   } else {
-    float* scores = reinterpret_cast<float*>(sb + off_scores);
     const int64_t n = T * E;
     router::route_f32_scores_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
         static_cast<const float*>(x), static_cast<const float*>(gate), bias, (int32_t)T, d, E, scores);
-    const size_t smem = (size_t)(k * tpb / 32) * E * 4;
-    router::topk_from_scores_kernel<<<(unsigned)nblk, router::kTopkTPB, smem, s>>>(scores, scales, (int32_t)T, E,
-                                                                                    k, ro);
+    CK(cudaGetLastError());
+    const size_t smem = router::topk_smem_bytes(E, k);
+    if (smem > 48 * 1024)
+      CK(cudaFuncSetAttribute(router::topk_from_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    router::topk_from_scores_kernel<<<(unsigned)nblk, router::kTopkTPB, smem, s>>>(scores, scales, (int32_t)T, E, k,
+                                                                                    ro, nofs);
   }
   CK(cudaGetLastError());
-  const int C = std::max(1, dispatch::kScanThreads / E);
-  dispatch::scan_segments_kernel<<<1, dispatch::kScanThreads, E * C * 4, s>>>(
+  dispatch::scan_segments_kernel<<<1, dispatch::kScanThreads, 0, s>>>(
       reinterpret_cast<const int32_t*>(sb + off_hist), (int32_t)nblk, E, tc::BM, counts,
       reinterpret_cast<int32_t*>(sb + off_seg), reinterpret_cast<int32_t*>(sb + off_base),
       reinterpret_cast<int32_t*>(sb + off_mt));

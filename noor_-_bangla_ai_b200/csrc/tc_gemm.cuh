@@ -13,13 +13,15 @@
 //   warp 0 lane 0 : TMA producer, STAGES-deep ring of (A, B) k-blocks in smem
 //   warp 1 lane 0 : tcgen05.mma issuer, M=128 x N=BN x K=16 per instruction,
 //                   f32 accumulator in TMEM, double-buffered (2 x BN columns)
-//   warps 2..5    : epilogue, tcgen05.ld TMEM -> registers -> activation ->
-//                   global; warp w reads TMEM lanes 32*(w%4) .. +31
+//   warps 2..9    : epilogue, tcgen05.ld TMEM -> registers -> activation ->
+//                   global; warp w reads TMEM lanes 32*(w%4) .. +31, warps
+//                   2..5 the first half of the tile's columns, 6..9 the second
 // Every mbarrier wait is bounded: after kWaitLimitCycles it records an error
 // code in the handle's device error word, raises a CTA-wide abort flag, and
 // all roles leave their loops; TMEM is always released before exit.
 //
-// No TMA multicast is used anywhere: every CTA loads its own tiles.
+// Every CTA loads its own tiles from global memory; no load is shared across
+// a cluster.
 #pragma once
 
 #include <cuda.h>
@@ -31,13 +33,15 @@ namespace tc {
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one 128B swizzle row
 constexpr int STAGES = 4;
-constexpr int NUM_THREADS = 192;
+constexpr int EPI_WARPS = 8;  // two warps per TMEM lane quarter, each on half the columns
+constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
 
 enum Epilogue : int {
   EPI_STORE_BF16 = 0,   // C = acc (bf16)
   EPI_STORE_F32 = 1,    // C = acc (f32)
   EPI_SWIGLU_BF16 = 2,  // C[:, j] = silu(acc[:, j]) * acc[:, BN/2 + j]   (per n-tile)
   EPI_GEGLU_BF16 = 3,   // C[:, j] = gelu_tanh(acc[:, j]) * acc[:, BN/2 + j]
+  EPI_COMBINE_BF16 = 4, // C[t, :] = (acc[t, :] + sum_i w[t,i] y[dst[t,i], :] (+ shared[t, :])) / sqrt 2
 };
 
 __host__ __device__ constexpr bool epi_gated(int e) { return e == EPI_SWIGLU_BF16 || e == EPI_GEGLU_BF16; }
@@ -66,6 +70,13 @@ struct Params {
   void* C;
   int64_t ldc;      // elements
   int* err;         // device error word
+  // EPI_COMBINE_BF16 only: the layer's gather-combine, fused into the dense
+  // branch's down projection (rows are tokens; acc is the dense output).
+  const bf16* y;          // [rows picked][ldc] expert outputs
+  const int32_t* dst_row; // [T][k]
+  const float* wts;       // [T][k]
+  const float* shared;    // [T][ldc] f32 shared-expert output, nullable
+  int32_t k;
 };
 
 // ---------------------------------------------------------------- PTX helpers
@@ -191,8 +202,8 @@ __device__ __forceinline__ void store_chunk32(void* C, int64_t ldc, int row, int
     for (int j = 0; j < 16; ++j) {
       float a = __uint_as_float(v[2 * j]), b = __uint_as_float(v[2 * j + 1]);
       if constexpr (EPI == EPI_SWIGLU_BF16) {
-        a = __fmul_rn(act_silu(a), __uint_as_float(u[2 * j]));
-        b = __fmul_rn(act_silu(b), __uint_as_float(u[2 * j + 1]));
+        a = __fmul_rn(act_silu_bf16out(a), __uint_as_float(u[2 * j]));
+        b = __fmul_rn(act_silu_bf16out(b), __uint_as_float(u[2 * j + 1]));
       } else if constexpr (EPI == EPI_GEGLU_BF16) {
         a = __fmul_rn(act_gelu_tanh(a), __uint_as_float(u[2 * j]));
         b = __fmul_rn(act_gelu_tanh(b), __uint_as_float(u[2 * j + 1]));
@@ -202,6 +213,108 @@ __device__ __forceinline__ void store_chunk32(void* C, int64_t ldc, int row, int
     uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(C) + (int64_t)row * ldc + col);
 #pragma unroll
     for (int j = 0; j < 4; ++j) dst[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+  }
+}
+
+// One 32-column chunk of the fused combine for token row `row`:
+// moe = sum_i w_i * y_i in rank order from zero, each multiply and add rounded
+// separately (moe.rs:159-165); (+ shared, moe.rs:168-173); out = (dense + moe)
+// * (1/sqrt 2) (parallel_ffn.rs:32-35).
+__device__ __forceinline__ void combine_chunk32(const Params& p, int row, int col, const uint32_t (&acc)[32],
+                                                const int32_t (&dst)[8], const float (&wv)[8]) {
+  float moe[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) moe[j] = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (i < p.k) {
+      const uint4* yp = reinterpret_cast<const uint4*>(p.y + (int64_t)dst[i] * p.ldc + col);
+      uint4 yv[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) yv[q] = __ldg(yp + q);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t u[4] = {yv[q].x, yv[q].y, yv[q].z, yv[q].w};
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          moe[8 * q + 2 * r] = __fadd_rn(moe[8 * q + 2 * r], __fmul_rn(wv[i], bf16_lo(u[r])));
+          moe[8 * q + 2 * r + 1] = __fadd_rn(moe[8 * q + 2 * r + 1], __fmul_rn(wv[i], bf16_hi(u[r])));
+        }
+      }
+    }
+  }
+  if (p.shared) {
+    const float4* sp = reinterpret_cast<const float4*>(p.shared + (int64_t)row * p.ldc + col);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 v = __ldg(sp + q);
+      moe[4 * q] = __fadd_rn(moe[4 * q], v.x);
+      moe[4 * q + 1] = __fadd_rn(moe[4 * q + 1], v.y);
+      moe[4 * q + 2] = __fadd_rn(moe[4 * q + 2], v.z);
+      moe[4 * q + 3] = __fadd_rn(moe[4 * q + 3], v.w);
+    }
+  }
+  const float inv_sqrt2 = 0x1.6a09e6p-1f;  // 1.0f32 / 2.0f32.sqrt()
+  uint32_t o[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float a = __fmul_rn(__fadd_rn(__uint_as_float(acc[2 * j]), moe[2 * j]), inv_sqrt2);
+    const float b = __fmul_rn(__fadd_rn(__uint_as_float(acc[2 * j + 1]), moe[2 * j + 1]), inv_sqrt2);
+    o[j] = pack_bf16(a, b);
+  }
+  uint4* dst_p = reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(p.C) + (int64_t)row * p.ldc + col);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) dst_p[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+}
+
+// Epilogue of one accumulator tile, run by one epilogue warp: TMEM lanes
+// 32*q .. +31 (the tile's rows row0 + 32*q + lane), column half `part`.
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t t_base, int32_t row0, int32_t rows, int32_t nt,
+                                              int q, int part, int lane) {
+  const int row_in_tile = q * 32 + lane;
+  const bool valid = row_in_tile < rows;
+  const int row = row0 + row_in_tile;
+  if constexpr (epi_gated(EPI)) {
+    constexpr int HALF = BN / 2;
+    constexpr int SPAN = HALF / 2;
+#pragma unroll 1
+    for (int c = part * SPAN; c < (part + 1) * SPAN; c += 32) {
+      uint32_t g[32], u[32];
+      tmem_ld32(t_base + c, g);
+      tmem_ld32(t_base + HALF + c, u);
+      tmem_ld_wait();
+      if (valid) store_chunk32<EPI>(p.C, p.ldc, row, nt * HALF + c, g, u);
+    }
+  } else if constexpr (EPI == EPI_COMBINE_BF16) {
+    constexpr int SPAN = BN / 2;
+    int32_t dst[8];
+    float wv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      dst[i] = 0;
+      wv[i] = 0.f;
+      if (valid && i < p.k) {
+        dst[i] = __ldg(p.dst_row + (int64_t)row * p.k + i);
+        wv[i] = __ldg(p.wts + (int64_t)row * p.k + i);
+      }
+    }
+#pragma unroll 1
+    for (int c = part * SPAN; c < (part + 1) * SPAN; c += 32) {
+      uint32_t g[32];
+      tmem_ld32(t_base + c, g);
+      tmem_ld_wait();
+      if (valid) combine_chunk32(p, row, nt * BN + c, g, dst, wv);
+    }
+  } else {
+    constexpr int SPAN = BN / 2;
+#pragma unroll 1
+    for (int c = part * SPAN; c < (part + 1) * SPAN; c += 32) {
+      uint32_t g[32];
+      tmem_ld32(t_base + c, g);
+      tmem_ld_wait();
+      if (valid) store_chunk32<EPI>(p.C, p.ldc, row, nt * BN + c, g, g);
+    }
   }
 }
 
@@ -236,7 +349,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&accf_bar[a], 1);
-      mbar_init(&acce_bar[a], 4);  // one arrive per epilogue warp
+      mbar_init(&acce_bar[a], EPI_WARPS);  // one arrive per epilogue warp
     }
     mbar_init(&drain_bar, 1);
     abort_flag = 0;
@@ -336,9 +449,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     __syncwarp();
   } else if (warp >= 2) {
-    // ---------------- epilogue: warp w owns TMEM lanes 32*(w%4) .. +31
+    // ---------------- epilogue: warp w owns TMEM lanes 32*(w%4) .. +31 and
+    // one half of the tile's columns
     const int q = warp & 3;
-    const int row_in_tile = q * 32 + lane;
+    const int part = (warp - 2) >> 2;  // 0: first half of the columns, 1: second
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int32_t tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
@@ -346,27 +460,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!mbar_wait(&accf_bar[acc], acc_phase, &abort_flag, p.err, DEV_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t t_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      const bool valid = row_in_tile < tc.rows;
-      const int row = tc.row0 + row_in_tile;
-      if constexpr (epi_gated(EPI)) {
-        constexpr int HALF = BN / 2;
-#pragma unroll 1
-        for (int c = 0; c < HALF; c += 32) {
-          uint32_t g[32], u[32];
-          tmem_ld32(t_base + c, g);
-          tmem_ld32(t_base + HALF + c, u);
-          tmem_ld_wait();
-          if (valid) store_chunk32<EPI>(p.C, p.ldc, row, tc.nt * HALF + c, g, u);
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t g[32];
-          tmem_ld32(t_base + c, g);
-          tmem_ld_wait();
-          if (valid) store_chunk32<EPI>(p.C, p.ldc, row, tc.nt * BN + c, g, g);
-        }
-      }
+      epilogue_tile<BN, EPI>(p, t_base, tc.row0, tc.rows, tc.nt, q, part, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce_bar[acc]);
@@ -381,6 +475,259 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::TMEM_COLS)
+                 : "memory");
+  }
+#endif
+}
+
+// ---------------------------------------------------------------- 2-CTA kernel
+//
+// The same GEMM on an SM pair (a cluster of two CTAs): one tcgen05.mma
+// .cta_group::2 computes a 256 x 256 x 16 tile, M split across the pair.
+// CTA r loads, with its own TMA copies, A rows [row0 + 128r, +128) and B rows
+// [n0 + 128r, +128) of the 256-column n-tile; the pair's MMA multiplies each
+// CTA's A half by both B halves, so each SM reads 8 KB of shared memory per
+// k16 step instead of 12 KB, for the same FLOPs.  Each CTA's TMEM holds its
+// own 128 x 256 accumulator rows, so the epilogue is the one-CTA epilogue.
+//
+// Synchronisation: both CTAs' TMA copies complete on the leader's (CTA 0)
+// full barrier; the leader alone issues MMAs and commits to the empty and
+// accumulator-full barriers of both CTAs; both CTAs' epilogue warps arrive on
+// the leader's accumulator-empty barrier.  Tiles are 256 rows: the group
+// table's tile numbering must use BM2 = 256.
+constexpr int BM2 = 256;
+constexpr int STAGES2 = 6;
+
+struct Cfg2 {
+  static constexpr int A_BYTES = 128 * BK * 2;  // this CTA's A half
+  static constexpr int B_BYTES = 128 * BK * 2;  // this CTA's B half
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SMEM_BYTES = STAGES2 * STAGE_BYTES + 1024;
+  static constexpr uint32_t TMEM_COLS = 512;  // two 256-column accumulators
+  static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
+                                    ((uint32_t)(256 >> 4) << 24);
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// TMA load into this CTA's shared memory whose completion is counted on the
+// leader CTA's barrier (clearing the peer bit of the barrier's address).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x,
+                                                 int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar) & 0xFEFFFFFFu), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on the barrier at this smem offset in both CTAs of the pair once the
+// MMAs issued so far retire.
+__device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar) {
+  const uint16_t mask = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_addr(bar)),
+      "h"(mask)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit_pair_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+// Arrive on the barrier at this smem offset in CTA `rank` of the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint64_t* bar, uint32_t rank) {
+  asm volatile(
+      "{\n\t.reg .b32 remAddr32;\n\t"
+      "mapa.shared::cluster.u32 remAddr32, %0, %1;\n\t"
+      "mbarrier.arrive.shared::cluster.b64 _, [remAddr32];\n\t}" ::"r"(smem_addr(bar)),
+      "r"(rank)
+      : "memory");
+}
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    grouped_gemm_2cta_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                             const Params p) {
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
+  using C = Cfg2;
+  constexpr int BN = 256;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + STAGES2 * C::A_BYTES;
+
+  __shared__ __align__(8) uint64_t full_bar[STAGES2];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES2];
+  __shared__ __align__(8) uint64_t accf_bar[2];
+  __shared__ __align__(8) uint64_t acce_bar[2];
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES2; ++s) {
+      mbar_init(&full_bar[s], 1);   // the leader's expect_tx; both CTAs' bytes
+      mbar_init(&empty_bar[s], 1);  // the leader's commit, delivered to both CTAs
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&accf_bar[a], 1);
+      mbar_init(&acce_bar[a], 2 * EPI_WARPS);  // epilogue warps of both CTAs (leader's copy is used)
+    }
+    mbar_init(&drain_bar, 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_slot)),
+                 "r"(C::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the peer's barriers exist before anyone signals them
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+
+  const int32_t nclusters = gridDim.x >> 1;
+  const int32_t cid = blockIdx.x >> 1;
+  const int32_t total_tiles = group_total_mtiles(p.groups, BM2) * p.n_tiles;
+  const int32_t num_kb = (p.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int32_t tile = cid; tile < total_tiles; tile += nclusters) {
+        const TileCoord tc = decode_tile(p.groups, tile, p.n_tiles, BM2);
+        const int32_t arow = tc.row0 + 128 * (int32_t)rank;
+        const int32_t brow = tc.widx * p.N + tc.nt * BN + 128 * (int32_t)rank;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, &abort_flag, p.err, DEV_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * C::STAGE_BYTES);
+          tma_load_2d_pair(smA + stage * C::A_BYTES, &tmA, &full_bar[stage], kb * BK, arow);
+          tma_load_2d_pair(smB + stage * C::B_BYTES, &tmB, &full_bar[stage], kb * BK, brow);
+          if (++stage == STAGES2) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (leader CTA only)
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool issued = false;
+      for (int32_t tile = cid; tile < total_tiles; tile += nclusters) {
+        if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1u, &abort_flag, p.err, DEV_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, &abort_flag, p.err, DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_addr(smA + stage * C::A_BYTES);
+          const uint32_t b0 = smem_addr(smB + stage * C::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_bf16_pair(d_tmem, sdesc_sw128(a0 + kk * 32), sdesc_sw128(b0 + kk * 32), C::IDESC,
+                           (kb | kk) != 0 ? 1u : 0u);
+          issued = true;
+          umma_commit_pair_both(&empty_bar[stage]);
+          if (++stage == STAGES2) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_both(&accf_bar[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (issued) {
+        umma_commit_pair_local(&drain_bar);
+        const long long start = clock64();
+        while (!mbar_try_wait(&drain_bar, 0) && clock64() - start < kWaitLimitCycles) {
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (both CTAs): this CTA's 128 rows of the pair tile
+    const int q = warp & 3;
+    const int part = (warp - 2) >> 2;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int32_t tile = cid; tile < total_tiles; tile += nclusters) {
+      const TileCoord tc = decode_tile(p.groups, tile, p.n_tiles, BM2);
+      if (!mbar_wait(&accf_bar[acc], acc_phase, &abort_flag, p.err, DEV_TIMEOUT_EPILOGUE)) break;
+      tc_fence_after();
+      const uint32_t t_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      epilogue_tile<BN, EPI>(p, t_base, tc.row0 + 128 * (int32_t)rank, tc.rows - 128 * (int32_t)rank, tc.nt, q,
+                             part, lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive(&acce_bar[acc]);
+        else mbar_arrive_cluster(&acce_bar[acc], 0);
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal it
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::TMEM_COLS)
                  : "memory");
   }
 #endif

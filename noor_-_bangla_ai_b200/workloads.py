@@ -223,12 +223,14 @@ def algorithmic_bytes(cfg: LayerConfig, tokens: int) -> dict:
     d, E, k = cfg.d_model, cfg.n_experts, cfg.top_k
     T = tokens
     return {
-        # x once, router gate once, idx + weight per pick, counts
-        "router": T * d * b + d * E * b + T * k * 8 + 8 * E,
+        # x once, router gate once, f32 scores written
+        "router_scores": T * d * b + d * E * b + T * E * 4,
+        # scores read; index, weight and rank per pick written
+        "router_topk": T * E * 4 + T * k * 12,
         # x once, k copies written, dst index per pick
         "permute": T * d * b + T * k * d * b + 8 * T * k,
-        # k expert rows + dense row read, out written, (index, weight) per pick
-        "combine": T * k * d * b + T * d * 4 + T * d * b + 8 * T * k,
+        # k expert rows gathered, out written, (index, weight) per pick
+        "combine": T * k * d * b + T * d * b + 8 * T * k,
     }
 
 

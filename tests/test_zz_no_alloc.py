@@ -12,6 +12,8 @@ It is named so that pytest collects it last.
 import numpy as np
 import pytest
 
+from tests import parity
+
 pytestmark = pytest.mark.gpu
 
 
@@ -64,11 +66,14 @@ def test_route_static_matches_route_twice(pkg, name):
     cfg = W.CONFIGS[name].with_tokens(3000)
     w, x, h, xd, gate, bias, scales = _setup(pkg, cfg)
     xin = W.bf16_bits(x) if cfg.dtype == W.BF16 else x
+    # the routing tolerance of the parity tests: picks and counts exact, weights
+    # within half the tie threshold
+    tol = (parity.TAU_BF16 if cfg.dtype == W.BF16 else parity.TAU_F32) / 2
     # first call: all 3000 tokens
     idx_ref, w_ref, c_ref = h.route_host(xin)
     idx, wt, counts, mem1 = _route_static(pkg, cfg, xd, gate, bias, scales, cfg.tokens)
     assert np.array_equal(idx, idx_ref)
-    assert np.array_equal(wt, w_ref)
+    np.testing.assert_allclose(wt, w_ref, rtol=0, atol=tol)
     assert np.array_equal(counts, c_ref)
     # second call right after, on a shorter batch: the array still holds the
     # first call's contents and must not leak into the result
@@ -76,7 +81,7 @@ def test_route_static_matches_route_twice(pkg, name):
     idx_ref2, w_ref2, c_ref2 = h.route_host(np.ascontiguousarray(xin[lo:hi]))
     idx2, wt2, counts2, mem2 = _route_static(pkg, cfg, xd[lo:hi].contiguous(), gate, bias, scales, hi - lo)
     assert np.array_equal(idx2, idx_ref2)
-    assert np.array_equal(wt2, w_ref2)
+    np.testing.assert_allclose(wt2, w_ref2, rtol=0, atol=tol)
     assert np.array_equal(counts2, c_ref2)
     assert int(counts2.sum()) == (hi - lo) * min(cfg.top_k, cfg.n_experts)
     assert mem1[0] == mem1[1] and mem2[0] == mem2[1]  # no device allocation inside the call
@@ -88,7 +93,7 @@ def test_route_static_rejects_oversized_batch(pkg):
     W = pkg.workloads
     cfg = W.CONFIGS["edge"].with_tokens(64)
     _w, _x, h, xd, gate, bias, scales = _setup(pkg, cfg)
-    T = 400000  # needs more than the fixed scratch; refused before any launch
+    T = 1000000  # needs more than the fixed 8 MiB scratch; refused before any launch
     with pytest.raises(pkg.api.NoorMoEError) as e:
         pkg.api.route_static(xd.data_ptr(), gate.data_ptr(), bias.data_ptr(), scales.data_ptr(), T, cfg.d_model,
                              cfg.n_experts, cfg.top_k, cfg.dtype, xd.data_ptr(), xd.data_ptr(), xd.data_ptr(),
