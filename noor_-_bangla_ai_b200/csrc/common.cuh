@@ -43,10 +43,11 @@ struct TileCoord {
 
 __device__ __forceinline__ int32_t group_total_mtiles(const GroupTable& gt, int BM) {
   if (gt.dense_rows >= 0) return (gt.dense_rows + BM - 1) / BM;
-  return __ldg(gt.mtile_start + gt.G);
+  return gt.mtile_start[gt.G];
 }
 
 // Map a flat tile id (m-tile major, n-tile minor) to its group coordinates.
+// The table pointers may point to global or shared memory.
 __device__ __forceinline__ TileCoord decode_tile(const GroupTable& gt, int32_t tile, int32_t n_tiles,
                                                  int BM) {
   TileCoord c;
@@ -62,15 +63,40 @@ __device__ __forceinline__ TileCoord decode_tile(const GroupTable& gt, int32_t t
   int lo = 0, hi = gt.G;  // invariant: mtile_start[lo] <= mt < mtile_start[hi]
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
-    if (__ldg(gt.mtile_start + mid) <= mt) lo = mid; else hi = mid;
+    if (gt.mtile_start[mid] <= mt) lo = mid; else hi = mid;
   }
-  const int32_t local = mt - __ldg(gt.mtile_start + lo);
-  const int32_t rs = __ldg(gt.row_start + lo);
-  const int32_t re = __ldg(gt.row_start + lo + 1);
+  const int32_t local = mt - gt.mtile_start[lo];
+  const int32_t rs = gt.row_start[lo];
+  const int32_t re = gt.row_start[lo + 1];
   c.row0 = rs + local * BM;
   c.rows = min(BM, re - c.row0);
-  c.widx = gt.weight_idx ? __ldg(gt.weight_idx + lo) : lo;
+  c.widx = gt.weight_idx ? gt.weight_idx[lo] : lo;
   return c;
+}
+
+// Copy a group table of up to kSmemGroups groups into shared memory
+// (s_tab: 3 * (kSmemGroups + 1) ints) so that per-tile decoding costs
+// shared-memory latency, not a chain of global loads; larger tables stay in
+// global memory.  All threads of the block call it; it ends with
+// __syncthreads().
+constexpr int kSmemGroups = 1024;
+__device__ __forceinline__ GroupTable stage_group_table(const GroupTable& gt, int32_t* s_tab) {
+  GroupTable out = gt;
+  if (gt.dense_rows < 0 && gt.G <= kSmemGroups) {
+    int32_t* rs = s_tab;
+    int32_t* mt = s_tab + (kSmemGroups + 1);
+    int32_t* wi = s_tab + 2 * (kSmemGroups + 1);
+    for (int i = threadIdx.x; i <= gt.G; i += blockDim.x) {
+      rs[i] = __ldg(gt.row_start + i);
+      mt[i] = __ldg(gt.mtile_start + i);
+      if (i < gt.G) wi[i] = gt.weight_idx ? __ldg(gt.weight_idx + i) : i;
+    }
+    out.row_start = rs;
+    out.mtile_start = mt;
+    out.weight_idx = wi;
+  }
+  __syncthreads();
+  return out;
 }
 
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }

@@ -187,6 +187,56 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 
 // ---------------------------------------------------------------- epilogue
 
+// Activation of one 32-column chunk of a row, packed to BF16 pairs.
+template <int EPI>
+__device__ __forceinline__ void activate_chunk32(const uint32_t (&v)[32], const uint32_t (&u)[32],
+                                                 uint32_t (&p)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    float a = __uint_as_float(v[2 * j]), b = __uint_as_float(v[2 * j + 1]);
+    if constexpr (EPI == EPI_SWIGLU_BF16) {
+      a = __fmul_rn(act_silu_bf16out(a), __uint_as_float(u[2 * j]));
+      b = __fmul_rn(act_silu_bf16out(b), __uint_as_float(u[2 * j + 1]));
+    } else if constexpr (EPI == EPI_GEGLU_BF16) {
+      a = __fmul_rn(act_gelu_tanh(a), __uint_as_float(u[2 * j]));
+      b = __fmul_rn(act_gelu_tanh(b), __uint_as_float(u[2 * j + 1]));
+    }
+    p[j] = pack_bf16(a, b);
+  }
+}
+
+// One thread writes its row's 32 BF16 values (64 bytes) straight to global.
+__device__ __forceinline__ void write_chunk32_direct(void* C, int64_t ldc, int row, int col, const uint32_t (&p)[16]) {
+  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(C) + (int64_t)row * ldc + col);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) dst[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+}
+
+// Warp-collective write of a 32-row x 32-column BF16 chunk (lane i holds row
+// row0 + i): the rows pass through a 2 KB shared-memory buffer (16-byte
+// pieces XOR-swizzled by (row >> 1) & 3, so both the row-wise writes and the
+// piece-wise reads are free of bank conflicts) and leave as 16-byte stores in
+// which 4 consecutive lanes cover one row's 64 bytes, 8 rows per instruction,
+// instead of 32 rows per instruction.  Rows >= rows_valid are not written.
+__device__ __forceinline__ void write_chunk32_staged(void* C, int64_t ldc, int row0, int rows_valid, int col,
+                                                     const uint32_t (&p)[16], uint8_t* stage, int lane) {
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    *reinterpret_cast<uint4*>(stage + lane * 64 + ((j ^ sw) << 4)) =
+        make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int piece = lane + 32 * j;
+    const int r = piece >> 2, part = piece & 3;
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + r * 64 + ((part ^ ((r >> 1) & 3)) << 4));
+    if (r < rows_valid)
+      *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(C) + (int64_t)(row0 + r) * ldc + col + part * 8) = v;
+  }
+  __syncwarp();  // the buffer is reused by the next chunk
+}
+
 template <int EPI>
 __device__ __forceinline__ void store_chunk32(void* C, int64_t ldc, int row, int col, const uint32_t (&v)[32],
                                               const uint32_t (&u)[32]) {
@@ -198,83 +248,73 @@ __device__ __forceinline__ void store_chunk32(void* C, int64_t ldc, int row, int
                            __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
   } else {
     uint32_t p[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      float a = __uint_as_float(v[2 * j]), b = __uint_as_float(v[2 * j + 1]);
-      if constexpr (EPI == EPI_SWIGLU_BF16) {
-        a = __fmul_rn(act_silu_bf16out(a), __uint_as_float(u[2 * j]));
-        b = __fmul_rn(act_silu_bf16out(b), __uint_as_float(u[2 * j + 1]));
-      } else if constexpr (EPI == EPI_GEGLU_BF16) {
-        a = __fmul_rn(act_gelu_tanh(a), __uint_as_float(u[2 * j]));
-        b = __fmul_rn(act_gelu_tanh(b), __uint_as_float(u[2 * j + 1]));
-      }
-      p[j] = pack_bf16(a, b);
-    }
-    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(C) + (int64_t)row * ldc + col);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) dst[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+    activate_chunk32<EPI>(v, u, p);
+    write_chunk32_direct(C, ldc, row, col, p);
   }
 }
 
-// One 32-column chunk of the fused combine for token row `row`:
-// moe = sum_i w_i * y_i in rank order from zero, each multiply and add rounded
-// separately (moe.rs:159-165); (+ shared, moe.rs:168-173); out = (dense + moe)
-// * (1/sqrt 2) (parallel_ffn.rs:32-35).
-__device__ __forceinline__ void combine_chunk32(const Params& p, int row, int col, const uint32_t (&acc)[32],
-                                                const int32_t (&dst)[8], const float (&wv)[8]) {
+// One 32-column chunk of the fused combine for token row `row`, packed to
+// BF16 pairs: moe = sum_i w_i * y_i in rank order from zero, each multiply and
+// add rounded separately (moe.rs:159-165); (+ shared, moe.rs:168-173);
+// out = (dense + moe) * (1/sqrt 2) (parallel_ffn.rs:32-35).
+__device__ __forceinline__ void combine_chunk32(const Params& p, int row, int col, bool valid,
+                                                const uint32_t (&acc)[32], const int32_t (&dst)[8],
+                                                const float (&wv)[8], uint32_t (&o)[16]) {
   float moe[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) moe[j] = 0.f;
+  if (valid) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    if (i < p.k) {
-      const uint4* yp = reinterpret_cast<const uint4*>(p.y + (int64_t)dst[i] * p.ldc + col);
-      uint4 yv[4];
+    for (int i = 0; i < 8; ++i) {
+      if (i < p.k) {
+        const uint4* yp = reinterpret_cast<const uint4*>(p.y + (int64_t)dst[i] * p.ldc + col);
+        uint4 yv[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) yv[q] = __ldg(yp + q);
+        for (int q = 0; q < 4; ++q) yv[q] = __ldg(yp + q);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint32_t u[4] = {yv[q].x, yv[q].y, yv[q].z, yv[q].w};
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t u[4] = {yv[q].x, yv[q].y, yv[q].z, yv[q].w};
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          moe[8 * q + 2 * r] = __fadd_rn(moe[8 * q + 2 * r], __fmul_rn(wv[i], bf16_lo(u[r])));
-          moe[8 * q + 2 * r + 1] = __fadd_rn(moe[8 * q + 2 * r + 1], __fmul_rn(wv[i], bf16_hi(u[r])));
+          for (int r = 0; r < 4; ++r) {
+            moe[8 * q + 2 * r] = __fadd_rn(moe[8 * q + 2 * r], __fmul_rn(wv[i], bf16_lo(u[r])));
+            moe[8 * q + 2 * r + 1] = __fadd_rn(moe[8 * q + 2 * r + 1], __fmul_rn(wv[i], bf16_hi(u[r])));
+          }
         }
       }
     }
-  }
-  if (p.shared) {
-    const float4* sp = reinterpret_cast<const float4*>(p.shared + (int64_t)row * p.ldc + col);
+    if (p.shared) {
+      const float4* sp = reinterpret_cast<const float4*>(p.shared + (int64_t)row * p.ldc + col);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 v = __ldg(sp + q);
-      moe[4 * q] = __fadd_rn(moe[4 * q], v.x);
-      moe[4 * q + 1] = __fadd_rn(moe[4 * q + 1], v.y);
-      moe[4 * q + 2] = __fadd_rn(moe[4 * q + 2], v.z);
-      moe[4 * q + 3] = __fadd_rn(moe[4 * q + 3], v.w);
+      for (int q = 0; q < 8; ++q) {
+        const float4 v = __ldg(sp + q);
+        moe[4 * q] = __fadd_rn(moe[4 * q], v.x);
+        moe[4 * q + 1] = __fadd_rn(moe[4 * q + 1], v.y);
+        moe[4 * q + 2] = __fadd_rn(moe[4 * q + 2], v.z);
+        moe[4 * q + 3] = __fadd_rn(moe[4 * q + 3], v.w);
+      }
     }
   }
   const float inv_sqrt2 = 0x1.6a09e6p-1f;  // 1.0f32 / 2.0f32.sqrt()
-  uint32_t o[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     const float a = __fmul_rn(__fadd_rn(__uint_as_float(acc[2 * j]), moe[2 * j]), inv_sqrt2);
     const float b = __fmul_rn(__fadd_rn(__uint_as_float(acc[2 * j + 1]), moe[2 * j + 1]), inv_sqrt2);
     o[j] = pack_bf16(a, b);
   }
-  uint4* dst_p = reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(p.C) + (int64_t)row * p.ldc + col);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) dst_p[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
 }
 
 // Epilogue of one accumulator tile, run by one epilogue warp: TMEM lanes
 // 32*q .. +31 (the tile's rows row0 + 32*q + lane), column half `part`.
+// With `stage` (2 KB of shared memory for this warp) BF16 outputs leave
+// through write_chunk32_staged; without it each thread stores its own row.
 template <int BN, int EPI>
 __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t t_base, int32_t row0, int32_t rows, int32_t nt,
-                                              int q, int part, int lane) {
+                                              int q, int part, int lane, uint8_t* stage) {
   const int row_in_tile = q * 32 + lane;
   const bool valid = row_in_tile < rows;
   const int row = row0 + row_in_tile;
+  const int wrow0 = row0 + q * 32;
+  const int wrows = max(0, min(32, rows - q * 32));
   if constexpr (epi_gated(EPI)) {
     constexpr int HALF = BN / 2;
     constexpr int SPAN = HALF / 2;
@@ -284,7 +324,10 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t t_base, 
       tmem_ld32(t_base + c, g);
       tmem_ld32(t_base + HALF + c, u);
       tmem_ld_wait();
-      if (valid) store_chunk32<EPI>(p.C, p.ldc, row, nt * HALF + c, g, u);
+      uint32_t pk[16];
+      activate_chunk32<EPI>(g, u, pk);
+      if (stage) write_chunk32_staged(p.C, p.ldc, wrow0, wrows, nt * HALF + c, pk, stage, lane);
+      else if (valid) write_chunk32_direct(p.C, p.ldc, row, nt * HALF + c, pk);
     }
   } else if constexpr (EPI == EPI_COMBINE_BF16) {
     constexpr int SPAN = BN / 2;
@@ -304,7 +347,10 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t t_base, 
       uint32_t g[32];
       tmem_ld32(t_base + c, g);
       tmem_ld_wait();
-      if (valid) combine_chunk32(p, row, nt * BN + c, g, dst, wv);
+      uint32_t pk[16];
+      combine_chunk32(p, row, nt * BN + c, valid, g, dst, wv, pk);
+      if (stage) write_chunk32_staged(p.C, p.ldc, wrow0, wrows, nt * BN + c, pk, stage, lane);
+      else if (valid) write_chunk32_direct(p.C, p.ldc, row, nt * BN + c, pk);
     }
   } else {
     constexpr int SPAN = BN / 2;
@@ -313,7 +359,14 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t t_base, 
       uint32_t g[32];
       tmem_ld32(t_base + c, g);
       tmem_ld_wait();
-      if (valid) store_chunk32<EPI>(p.C, p.ldc, row, nt * BN + c, g, g);
+      if constexpr (EPI == EPI_STORE_F32) {
+        if (valid) store_chunk32<EPI>(p.C, p.ldc, row, nt * BN + c, g, g);
+      } else {
+        uint32_t pk[16];
+        activate_chunk32<EPI>(g, g, pk);
+        if (stage) write_chunk32_staged(p.C, p.ldc, wrow0, wrows, nt * BN + c, pk, stage, lane);
+        else if (valid) write_chunk32_direct(p.C, p.ldc, row, nt * BN + c, pk);
+      }
     }
   }
 }
@@ -369,7 +422,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
 
-  const int32_t total_tiles = group_total_mtiles(p.groups, BM) * p.n_tiles;
+  __shared__ int32_t s_tab[3 * (kSmemGroups + 1)];
+  const GroupTable groups = stage_group_table(p.groups, s_tab);
+  const int32_t total_tiles = group_total_mtiles(groups, BM) * p.n_tiles;
   const int32_t num_kb = (p.K + BK - 1) / BK;
 
   if (warp == 0) {
@@ -378,7 +433,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int stage = 0;
     uint32_t phase = 0;
     for (int32_t tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
-      const TileCoord tc = decode_tile(p.groups, tile, p.n_tiles, BM);
+      const TileCoord tc = decode_tile(groups, tile, p.n_tiles, BM);
       const int32_t brow = tc.widx * p.N + tc.nt * BN;
       bool ok = true;
       for (int kb = 0; kb < num_kb; ++kb) {
@@ -456,11 +511,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int32_t tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
-      const TileCoord tc = decode_tile(p.groups, tile, p.n_tiles, BM);
+      const TileCoord tc = decode_tile(groups, tile, p.n_tiles, BM);
       if (!mbar_wait(&accf_bar[acc], acc_phase, &abort_flag, p.err, DEV_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t t_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      epilogue_tile<BN, EPI>(p, t_base, tc.row0, tc.rows, tc.nt, q, part, lane);
+      epilogue_tile<BN, EPI>(p, t_base, tc.row0, tc.rows, tc.nt, q, part, lane, nullptr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce_bar[acc]);
@@ -496,13 +551,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // the leader's accumulator-empty barrier.  Tiles are 256 rows: the group
 // table's tile numbering must use BM2 = 256.
 constexpr int BM2 = 256;
-constexpr int STAGES2 = 6;
+constexpr int STAGES2 = 5;
 
 struct Cfg2 {
   static constexpr int A_BYTES = 128 * BK * 2;  // this CTA's A half
   static constexpr int B_BYTES = 128 * BK * 2;  // this CTA's B half
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int SMEM_BYTES = STAGES2 * STAGE_BYTES + 1024;
+  static constexpr int STAGE_OUT_BYTES = 2048;  // per epilogue warp, write_chunk32_staged
+  static constexpr int SMEM_BYTES = STAGES2 * STAGE_BYTES + EPI_WARPS * STAGE_OUT_BYTES + 1024;
   static constexpr uint32_t TMEM_COLS = 512;  // two 256-column accumulators
   static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
                                     ((uint32_t)(256 >> 4) << 24);
@@ -576,6 +632,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smA = smem;
   uint8_t* smB = smem + STAGES2 * C::A_BYTES;
+  uint8_t* smOut = smem + STAGES2 * C::STAGE_BYTES;  // EPI_WARPS x 2 KB
 
   __shared__ __align__(8) uint64_t full_bar[STAGES2];
   __shared__ __align__(8) uint64_t empty_bar[STAGES2];
@@ -620,7 +677,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 
   const int32_t nclusters = gridDim.x >> 1;
   const int32_t cid = blockIdx.x >> 1;
-  const int32_t total_tiles = group_total_mtiles(p.groups, BM2) * p.n_tiles;
+  __shared__ int32_t s_tab[3 * (kSmemGroups + 1)];
+  const GroupTable groups = stage_group_table(p.groups, s_tab);
+  const int32_t total_tiles = group_total_mtiles(groups, BM2) * p.n_tiles;
   const int32_t num_kb = (p.K + BK - 1) / BK;
 
   if (warp == 0) {
@@ -629,7 +688,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int32_t tile = cid; tile < total_tiles; tile += nclusters) {
-        const TileCoord tc = decode_tile(p.groups, tile, p.n_tiles, BM2);
+        const TileCoord tc = decode_tile(groups, tile, p.n_tiles, BM2);
         const int32_t arow = tc.row0 + 128 * (int32_t)rank;
         const int32_t brow = tc.widx * p.N + tc.nt * BN + 128 * (int32_t)rank;
         bool ok = true;
@@ -704,12 +763,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int32_t tile = cid; tile < total_tiles; tile += nclusters) {
-      const TileCoord tc = decode_tile(p.groups, tile, p.n_tiles, BM2);
+      const TileCoord tc = decode_tile(groups, tile, p.n_tiles, BM2);
       if (!mbar_wait(&accf_bar[acc], acc_phase, &abort_flag, p.err, DEV_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t t_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       epilogue_tile<BN, EPI>(p, t_base, tc.row0 + 128 * (int32_t)rank, tc.rows - 128 * (int32_t)rank, tc.nt, q,
-                             part, lane);
+                             part, lane, smOut + (warp - 2) * C::STAGE_OUT_BYTES);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
