@@ -242,12 +242,13 @@ def run_ours(args):
         step()
     barrier()
 
-    # One GPU: the timed steps replay one captured forward (a CUDA graph);
-    # under expert parallelism the forward waits on the host for the exchange
-    # plan, so the steps are plain calls.
+    # The timed steps replay one captured forward (a CUDA graph) on one GPU
+    # and under expert parallelism over peer memory; the NCCL exchange waits
+    # on the host for its plan, so there the steps are plain calls.
+    transport = h.ep_transport
     graph = None
     launches_per_step = None
-    if world == 1 and not args.no_graph:
+    if transport in ("none", "peer") and not args.no_graph:
         cs = torch.cuda.Stream(dev)
         cs.wait_stream(stream)
         with torch.cuda.stream(cs):
@@ -354,7 +355,7 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": tot_ms / args.steps, "higher_is_better": True,
             "scaling": scaling, "vs_baseline": None, "dtype": "bf16" if cfg.dtype == W.BF16 else "f32",
             "data": "synthetic (seeded Philox; x = RMSNorm(N(0,1)), weights N(0,0.02), bias U(-0.1,0.1))",
-            "config": config_dict(cfg, T, world, scaling),
+            "config": dict(config_dict(cfg, T, world, scaling), ep_transport=transport),
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes,
                     "api": "noor_moe_forward (device mode) with pinned-host H2D/D2H in the timed region"},
             "gpu_launches": launches,

@@ -156,6 +156,28 @@ NOOR_MOE_API int noor_moe_ep_plan(const int64_t* counts_local, const int64_t* co
                                   int64_t* send_rows, int64_t* send_off, int64_t* recv_rows, int64_t* recv_off,
                                   int32_t* grp_row, int32_t* grp_mtile, int32_t* grp_widx);
 
+/* How a handle's ranks exchange rows (no counterpart in the reference, which
+ * runs on one device).  With world_size > 1, noor_moe_create is collective
+ * and picks, the same on every rank:
+ *   NOOR_MOE_EP_PEER  BF16 layers whose GPUs all reach each other: the rows
+ *       move through the ranks' buffers mapped with CUDA IPC (NVLink stores
+ *       from the permute and from the expert down projection's epilogue),
+ *       synchronised by bounded device-side flag barriers; no host sync
+ *       inside a forward.  Each rank's T may not exceed the largest
+ *       max_tokens given at creation: a larger batch returns
+ *       NOOR_MOE_ERR_INVALID on its rank and every rank skips that step
+ *       (the others report it as NOOR_MOE_ERR_INVALID from the device).  A
+ *       rank that waits longer than NOOR_MOE_PEER_TIMEOUT_MS (environment,
+ *       default 10000) for another returns NOOR_MOE_ERR_TIMEOUT and the
+ *       exchange stays closed for the handle.
+ *   NOOR_MOE_EP_NCCL  otherwise (or NOOR_MOE_EP_TRANSPORT=nccl): a count
+ *       exchange, a host-built plan and NCCL all-to-all-v.
+ * Returns NOOR_MOE_EP_NONE for a single-GPU handle, -1 for NULL. */
+#define NOOR_MOE_EP_NONE 0
+#define NOOR_MOE_EP_NCCL 1
+#define NOOR_MOE_EP_PEER 2
+NOOR_MOE_API int noor_moe_ep_transport(const noor_moe_handle* h);
+
 /* ---- measurement hooks (CUDA events on the launching stream) ---- */
 
 /* Begin recording a start/stop event pair around every kernel the handle

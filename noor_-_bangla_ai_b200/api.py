@@ -38,8 +38,10 @@ EXPORTED_SYMBOLS = (
     "noor_moe_route", "noor_matmul_f32", "noor_moe_last_error", "noor_moe_sync", "noor_moe_destroy",
     "noor_moe_comm_id_size", "noor_moe_comm_get_id", "noor_moe_comm_init_rank",
     "noor_moe_comm_destroy", "noor_moe_profile_begin", "noor_moe_profile_end",
-    "noor_moe_launch_count", "noor_moe_ep_plan", "noor_moe_route_static",
+    "noor_moe_launch_count", "noor_moe_ep_plan", "noor_moe_route_static", "noor_moe_ep_transport",
 )
+
+EP_TRANSPORTS = {0: "none", 1: "nccl", 2: "peer"}
 
 
 class NoorMoEError(RuntimeError):
@@ -94,6 +96,8 @@ def lib() -> ctypes.CDLL:
                                        ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
     L.noor_moe_launch_count.argtypes = [_vp]
     L.noor_moe_launch_count.restype = ctypes.c_int64
+    L.noor_moe_ep_transport.argtypes = [_vp]
+    L.noor_moe_ep_transport.restype = ctypes.c_int
     L.noor_moe_route_static.argtypes = [_vp, _vp, _vp, _vp, _i64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                         ctypes.c_int32, _vp, _vp, _vp, _vp]
     _lib = L
@@ -207,6 +211,11 @@ class Handle:
 
     def launch_count(self) -> int:
         return int(lib().noor_moe_launch_count(self._h))
+
+    @property
+    def ep_transport(self) -> str:
+        """How the ranks exchange rows: "none" (one GPU), "nccl" or "peer"."""
+        return EP_TRANSPORTS.get(int(lib().noor_moe_ep_transport(self._h)), "?")
 
     def profile_begin(self, max_launches: int) -> None:
         check(lib().noor_moe_profile_begin(self._h, max_launches))

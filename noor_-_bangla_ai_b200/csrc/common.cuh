@@ -17,6 +17,8 @@ enum DevError : int {
   DEV_TIMEOUT_MMA = 2,
   DEV_TIMEOUT_EPILOGUE = 3,
   DEV_BAD_INDEX = 4,
+  DEV_TIMEOUT_PEER = 5,  // a wait on another rank gave up
+  DEV_PEER_PLAN = 6,     // the expert-parallel plan was refused (over-capacity batch)
 };
 
 // ~2 s at the B200's 1.9 GHz boost clock; no healthy wait comes close.
@@ -39,6 +41,7 @@ struct TileCoord {
   int32_t rows;   // valid rows (<= BM)
   int32_t widx;   // weight matrix index
   int32_t nt;     // n-tile index
+  int32_t g;      // group index (0 for a dense table)
 };
 
 __device__ __forceinline__ int32_t group_total_mtiles(const GroupTable& gt, int BM) {
@@ -57,6 +60,7 @@ __device__ __forceinline__ TileCoord decode_tile(const GroupTable& gt, int32_t t
     c.row0 = mt * BM;
     c.rows = min(BM, gt.dense_rows - c.row0);
     c.widx = 0;
+    c.g = 0;
     return c;
   }
   // last g with mtile_start[g] <= mt (groups with no tiles are skipped)
@@ -71,6 +75,7 @@ __device__ __forceinline__ TileCoord decode_tile(const GroupTable& gt, int32_t t
   c.row0 = rs + local * BM;
   c.rows = min(BM, re - c.row0);
   c.widx = gt.weight_idx ? gt.weight_idx[lo] : lo;
+  c.g = lo;
   return c;
 }
 

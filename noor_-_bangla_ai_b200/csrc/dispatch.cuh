@@ -99,42 +99,46 @@ __global__ void __launch_bounds__(kScanThreads) scan_segments_kernel(const int32
 
 // ------------------------------------------------------------------ permute
 
-// One warp per token: read the token's row once with 16-byte loads and write
-// it to the row of each of its k picks; record that row in dst_row[t, slot].
-constexpr int kPermuteWarps = 8;
+// Each warp takes tokens in a grid-stride loop: it reads the token's row once
+// (up to 4 KB in one batch of 16-byte loads) and writes it to the row of each
+// of its k picks, recording that row in dst_row[t, slot].  Launched either
+// with a block per 4 tokens, or persistent with one 4-warp block per SM
+// (48 registers a thread) beside a tensor-core GEMM that holds the rest of
+// each SM.
+constexpr int kPermuteWarps = 4;
 
 __global__ void __launch_bounds__(kPermuteWarps * 32) permute_rows_kernel(
     const uint8_t* __restrict__ x, int32_t row_bytes, int32_t T, int32_t k, int32_t nblk, int32_t tpb,
     const int32_t* __restrict__ idx, const int32_t* __restrict__ lrank, const int32_t* __restrict__ blk_base,
     uint8_t* __restrict__ xp, int32_t* __restrict__ dst_row) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int32_t t = blockIdx.x * kPermuteWarps + warp;
-  if (t >= T) return;
-  int32_t dst[8];
-  const int32_t* bb = blk_base + t / tpb;  // blk_base[e][block] is bb[e * nblk]
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    if (i < k) {
-      const int32_t e = __ldg(idx + (int64_t)t * k + i);
-      dst[i] = __ldg(bb + (int64_t)e * nblk) + __ldg(lrank + (int64_t)t * k + i);
-      if (lane == 0) dst_row[(int64_t)t * k + i] = dst[i];
-    }
-  }
   const int nvec = row_bytes >> 4;
-  const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)t * row_bytes);
-  constexpr int U = 4;
-  for (int base = lane; base < nvec; base += 32 * U) {
-    uint4 v[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u)
-      if (base + 32 * u < nvec) v[u] = __ldg(src + base + 32 * u);
+  constexpr int U = 8;
+  for (int32_t t = blockIdx.x * kPermuteWarps + warp; t < T; t += gridDim.x * kPermuteWarps) {
+    int32_t dst[8];
+    const int32_t* bb = blk_base + t / tpb;  // blk_base[e][block] is bb[e * nblk]
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       if (i < k) {
-        uint4* d = reinterpret_cast<uint4*>(xp + (int64_t)dst[i] * row_bytes);
+        const int32_t e = __ldg(idx + (int64_t)t * k + i);
+        dst[i] = __ldg(bb + (int64_t)e * nblk) + __ldg(lrank + (int64_t)t * k + i);
+        if (lane == 0) dst_row[(int64_t)t * k + i] = dst[i];
+      }
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)t * row_bytes);
+    for (int base = lane; base < nvec; base += 32 * U) {
+      uint4 v[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-          if (base + 32 * u < nvec) d[base + 32 * u] = v[u];
+      for (int u = 0; u < U; ++u)
+        if (base + 32 * u < nvec) v[u] = __ldg(src + base + 32 * u);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i < k) {
+          uint4* d = reinterpret_cast<uint4*>(xp + (int64_t)dst[i] * row_bytes);
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (base + 32 * u < nvec) d[base + 32 * u] = v[u];
+        }
       }
     }
   }

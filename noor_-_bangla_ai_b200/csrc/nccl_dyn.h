@@ -24,6 +24,7 @@ struct NcclApi {
   ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                             cudaStream_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
   bool ok = false;
 };
@@ -46,10 +47,11 @@ inline const NcclApi& nccl() {
     NOOR_NCCL_SYM(Send, "ncclSend");
     NOOR_NCCL_SYM(Recv, "ncclRecv");
     NOOR_NCCL_SYM(AllReduce, "ncclAllReduce");
+    NOOR_NCCL_SYM(AllGather, "ncclAllGather");
     NOOR_NCCL_SYM(GetErrorString, "ncclGetErrorString");
 #undef NOOR_NCCL_SYM
     api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.CommAbort && api.GroupStart &&
-             api.GroupEnd && api.Send && api.Recv && api.AllReduce && api.GetErrorString;
+             api.GroupEnd && api.Send && api.Recv && api.AllReduce && api.AllGather && api.GetErrorString;
   });
   return api;
 }

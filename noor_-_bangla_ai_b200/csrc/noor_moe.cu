@@ -5,13 +5,14 @@
 //   K1  router            x -> top-k idx / weights, per-block ranks + histogram
 //   scan                  histograms -> expert segments, per-block bases, GEMM tile table
 //   K2  permute           x rows -> expert-contiguous rows (dst_row per pick)
-//   [EP] count exchange + all-to-all-v of the rows (NCCL send/recv), so each
-//        rank holds the rows of its own experts
+//   [EP] the rows go to the rank that owns their expert: over NVLink peer
+//        memory (BF16: the permute stores into the owner's receive buffer,
+//        the down projection's epilogue stores the outputs back), else as a
+//        count exchange + all-to-all-v through NCCL send/recv
 //   K3  expert GEMM 1     rows . [Wg|Wu]^T  -> silu(g)*u      (tcgen05, SwiGLU epilogue)
 //   K3  expert GEMM 2     h . Wd^T          -> y
-//   [EP] reverse all-to-all-v of y
-//   dense branch          x . [Wg|Wu]^T -> gelu(g)*u -> . Wd^T   (second stream)
-//   K4  combine           out = (dense + sum_i w_i y_i) / sqrt(2)
+//   dense branch          x . [Wg|Wu]^T -> gelu(g)*u -> . Wd^T
+//   K4  combine           out = (dense + sum_i w_i y_i) / sqrt(2)   (the dense down projection's epilogue)
 // which is ParallelFFN::forward (crates/noor-core/src/layers/parallel_ffn.rs:30-36)
 // over MoELayer::forward (moe.rs:145-177).
 #include <cuda.h>
@@ -22,17 +23,21 @@
 #include <chrono>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <mutex>
 #include <thread>
 #include <vector>
 
+#include <unistd.h>
+
 #include "noor_moe.h"
 
 #include "common.cuh"
 #include "dispatch.cuh"
 #include "nccl_dyn.h"
+#include "peer_ep.cuh"
 #include "prepack.cuh"
 #include "router.cuh"
 #include "simt_gemm.cuh"
@@ -143,12 +148,12 @@ static int encode_kmajor(CUtensorMap* m, const void* base, int64_t rows, int64_t
 enum KernelKind : int {
   K_ROUTER = 0, K_ROUTER_SCORES, K_ROUTER_TOPK, K_SCAN, K_PERMUTE, K_EXPERT_GEMM1, K_EXPERT_GEMM2,
   K_DENSE_GEMM1, K_DENSE_GEMM2, K_SHARED_GEMM1, K_SHARED_GEMM2, K_COMBINE, K_PREPACK, K_A2A_DISPATCH,
-  K_A2A_COMBINE, K_COUNT_EXCHANGE, K_MATMUL, K_NUM
+  K_A2A_COMBINE, K_COUNT_EXCHANGE, K_MATMUL, K_EP_PLAN, K_EP_BARRIER, K_NUM
 };
 static const char* kKindNames[K_NUM] = {
     "router", "router_scores", "router_topk", "scan", "permute", "expert_gemm1", "expert_gemm2",
     "dense_gemm1", "dense_gemm2", "shared_gemm1", "shared_gemm2", "combine", "prepack",
-    "a2a_dispatch", "a2a_combine", "count_exchange", "matmul"};
+    "a2a_dispatch", "a2a_combine", "count_exchange", "matmul", "ep_plan", "ep_barrier"};
 
 // ============================================================== handle
 
@@ -184,6 +189,17 @@ struct noor_moe_handle {
   DevBuf xp, h, y, xrecv, ysend;
   DevBuf dense_h, dense_out, shared_h, shared_out;
   DevBuf grp_row, grp_mtile, grp_widx, cnt_recv;
+  // expert parallelism over peer memory (BF16 layers whose GPUs reach each
+  // other): buffers the other ranks store into, sized once for capP tokens
+  // per rank and never reallocated, since the other ranks hold mappings.
+  bool peer = false;
+  int64_t capP = 0;                 // tokens per rank (the largest max_tokens of all ranks)
+  DevBuf pxrecv, py, psync;         // receive rows | returned expert outputs | flags + counts
+  DevBuf pseq, pstatus, dest_base, grp_orank, grp_oshift;
+  noor::peer::Peers peers{};
+  void* peer_y[noor::peer::kMaxRanks] = {};
+  std::vector<void*> ipc_opened;    // mappings of other processes' buffers, closed on destroy
+  CUtensorMap tm_pxrecv{};
   int64_t* h_cnt = nullptr;  // pinned [E + G*El]
   int32_t* h_grp = nullptr;  // pinned [3 * (G*El + 1)]
   CUtensorMap tm_xp{}, tm_xrecv{}, tm_h{}, tm_xin{}, tm_dh{}, tm_sh{};
@@ -314,11 +330,17 @@ int wait_event_deadline(noor_moe_handle* h, cudaEvent_t ev, double seconds) {
 int check_device_error(noor_moe_handle* h) {
   int err = 0;
   CK(cudaMemcpy(&err, h->d_err, sizeof(int), cudaMemcpyDeviceToHost));
-  if (err != 0) {
-    cudaMemset(h->d_err, 0, sizeof(int));
-    return fail(NOOR_MOE_ERR_TIMEOUT, "a kernel's bounded wait gave up (device code %d)", err);
+  if (err == 0) return NOOR_MOE_OK;
+  cudaMemset(h->d_err, 0, sizeof(int));
+  if (err == noor::DEV_PEER_PLAN)
+    return fail(NOOR_MOE_ERR_INVALID, "a rank's batch exceeded the expert-parallel capacity; every rank skipped "
+                "this step");
+  if (err == noor::DEV_TIMEOUT_PEER) {
+    // the ranks' barrier counters may now disagree: no further exchange
+    h->comm_broken = true;
+    return fail(NOOR_MOE_ERR_TIMEOUT, "a wait on another rank gave up; the expert-parallel exchange is closed");
   }
-  return NOOR_MOE_OK;
+  return fail(NOOR_MOE_ERR_TIMEOUT, "a kernel's bounded wait gave up (device code %d)", err);
 }
 
 int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
@@ -346,11 +368,13 @@ int ensure_workspace(noor_moe_handle* h, int64_t T) {
   CKR(h->seg_start.ensure((h->E + 1) * 4));
   CKR(h->mtile_start.ensure((h->E + 1) * 4));
   if (!h->bf16) CKR(h->scores.ensure(capT * h->E * 4));
-  CKR(h->xp.ensure(Rl * d * b));
   CKR(h->h.ensure(Rr * h->ff * b));
-  CKR(h->y.ensure(Rr * d * b));
   h->cap_recv = std::max(h->cap_recv, Rr);
-  if (h->G > 1) {
+  if (!h->peer) {
+    CKR(h->xp.ensure(Rl * d * b));
+    CKR(h->y.ensure(Rr * d * b));
+  }
+  if (h->G > 1 && !h->peer) {
     CKR(h->xrecv.ensure(Rr * d * b));
     CKR(h->ysend.ensure(Rl * d * b));
     const int ng = h->G * h->El;
@@ -368,8 +392,8 @@ int ensure_workspace(noor_moe_handle* h, int64_t T) {
     CKR(h->shared_out.ensure(capT * d * 4));
   }
   if (h->bf16) {
-    CKR(encode_kmajor(&h->tm_xp, h->xp.p, Rl, d, tc::BM));
-    if (h->G > 1) CKR(encode_kmajor(&h->tm_xrecv, h->xrecv.p, h->cap_recv, d, tc::BM));
+    if (!h->peer) CKR(encode_kmajor(&h->tm_xp, h->xp.p, Rl, d, tc::BM));
+    if (h->G > 1 && !h->peer) CKR(encode_kmajor(&h->tm_xrecv, h->xrecv.p, h->cap_recv, d, tc::BM));
     CKR(encode_kmajor(&h->tm_h, h->h.p, h->cap_recv, h->ff, tc::BM));
     CKR(encode_kmajor(&h->tm_xin, h->x_in.p, capT, d, tc::BM));
     if (h->has_dense) CKR(encode_kmajor(&h->tm_dh, h->dense_h.p, capT, h->dff, tc::BM));
@@ -407,6 +431,21 @@ struct CombineArgs {
   int32_t k;
 };
 
+// Expert parallelism over peer memory: the store epilogue sends group g's
+// rows to rank rank[g]'s buffer bases[rank[g]] at row + shift[g].
+struct PeerOut {
+  const int32_t* rank;
+  const int32_t* shift;
+  void* const* bases;
+};
+
+void set_peer_out(tc::Params& p, const PeerOut* po) {
+  if (!po) return;
+  p.out_rank = po->rank;
+  p.out_shift = po->shift;
+  for (int r = 0; r < noor::peer::kMaxRanks; ++r) p.out_peer[r] = po->bases[r];
+}
+
 // Raise a kernel's dynamic shared-memory limit to at least `bytes`.  Up to
 // 48 KB needs no attribute; above it the limit set so far for each
 // (kernel, device) is remembered, so the slow host call runs only when a
@@ -440,7 +479,7 @@ int ensure_smem_limit(K kern, int bytes) {
 template <int BN, int EPI>
 int launch_tc(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& tA, const CUtensorMap& tB,
               const GroupTable& gt, int N, int K, void* C, int64_t ldc, int64_t max_mtiles,
-              const CombineArgs* comb = nullptr) {
+              const CombineArgs* comb = nullptr, const PeerOut* po = nullptr) {
   using Cf = tc::Cfg<BN>;
   auto kern = tc::grouped_gemm_kernel<BN, EPI>;
   CKR(ensure_smem_limit(kern, Cf::SMEM_BYTES));
@@ -459,6 +498,7 @@ int launch_tc(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& t
     p.shared = comb->shared;
     p.k = comb->k;
   }
+  set_peer_out(p, po);
   const int64_t tiles = std::max<int64_t>(1, max_mtiles * p.n_tiles);
   const int grid = (int)std::min<int64_t>(h->num_sms, tiles);
   return launch(h, s, kind, [&] { kern<<<grid, tc::NUM_THREADS, Cf::SMEM_BYTES, s>>>(tA, tB, p); });
@@ -467,7 +507,7 @@ int launch_tc(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& t
 template <int EPI>
 int launch_tc2(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& tA, const CUtensorMap& tB,
                const GroupTable& gt, int N, int K, void* C, int64_t ldc, int64_t max_tiles,
-               const CombineArgs* comb = nullptr) {
+               const CombineArgs* comb = nullptr, const PeerOut* po = nullptr) {
   auto kern = tc::grouped_gemm_2cta_kernel<EPI>;
   CKR(ensure_smem_limit(kern, tc::Cfg2::SMEM_BYTES));
   tc::Params p{};
@@ -485,6 +525,7 @@ int launch_tc2(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& 
     p.shared = comb->shared;
     p.k = comb->k;
   }
+  set_peer_out(p, po);
   const int64_t tiles = std::max<int64_t>(1, max_tiles * p.n_tiles);
   const int clusters = (int)std::min<int64_t>(h->num_sms / 2, tiles);
   return launch(h, s, kind, [&] { kern<<<2 * clusters, tc::NUM_THREADS, tc::Cfg2::SMEM_BYTES, s>>>(tA, tB, p); });
@@ -497,13 +538,13 @@ int launch_tc2(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& 
 template <int EPI>
 int launch_gemm(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& tA, const CUtensorMap& tB,
                 const GroupTable& gt, int N, int K, void* C, int64_t ldc, int64_t max_tiles,
-                const CombineArgs* comb = nullptr) {
-  if (h->pair2) return launch_tc2<EPI>(h, s, kind, tA, tB, gt, N, K, C, ldc, max_tiles, comb);
-  if (N % 256 == 0) return launch_tc<256, EPI>(h, s, kind, tA, tB, gt, N, K, C, ldc, max_tiles, comb);
+                const CombineArgs* comb = nullptr, const PeerOut* po = nullptr) {
+  if (h->pair2) return launch_tc2<EPI>(h, s, kind, tA, tB, gt, N, K, C, ldc, max_tiles, comb, po);
+  if (N % 256 == 0) return launch_tc<256, EPI>(h, s, kind, tA, tB, gt, N, K, C, ldc, max_tiles, comb, po);
   if constexpr (tc::epi_gated(EPI)) {
     return fail(NOOR_MOE_ERR_UNSUPPORTED, "gated GEMM needs N a multiple of 256");
   } else {
-    return launch_tc<128, EPI>(h, s, kind, tA, tB, gt, N, K, C, ldc, max_tiles, comb);
+    return launch_tc<128, EPI>(h, s, kind, tA, tB, gt, N, K, C, ldc, max_tiles, comb, po);
   }
 }
 
@@ -711,6 +752,305 @@ int ep_exchange(noor_moe_handle* h, cudaStream_t s, int kind, const EpPlan& plan
   });
 }
 
+// ============================================================== expert parallel over peer memory
+
+// Whether the side branches (dense up projection, shared expert) run on a
+// second stream beside the permute.  Measured on B200 with the Edge layer
+// (16384 tokens a GPU), running them in line is faster both on one GPU
+// (1.26 ms against 1.40 ms a step) and under expert parallelism over peer
+// memory on two GPUs (1.38 ms against 1.43 ms): the permute's copies take
+// L2 bandwidth the dense GEMM needs, and the expert GEMM still waits for the
+// dense GEMM's SMs, so the overlap costs more than the hidden copy time.
+constexpr bool kForkSideSingle = false;
+constexpr bool kForkSidePeer = false;
+
+// Wait, bounded, for the setup collectives queued on the handle's stream.
+int setup_sync(noor_moe_handle* h) {
+  CK(cudaEventRecord(h->ev_done, h->own));
+  return wait_event_deadline(h, h->ev_done, 120.0);
+}
+
+// Minimum of v over the ranks (setup only).
+int allreduce_min(noor_moe_handle* h, int64_t* v) {
+  DevBuf t;
+  CKR(t.ensure(16));
+  CK(cudaMemcpy(t.p, v, 8, cudaMemcpyHostToDevice));
+  CKN(noor::nccl().AllReduce(t.p, t.as<int64_t>() + 1, 1, ncclInt64, ncclMin, h->comm, h->own));
+  CKR(setup_sync(h));
+  CK(cudaMemcpy(v, t.as<int64_t>() + 1, 8, cudaMemcpyDeviceToHost));
+  return NOOR_MOE_OK;
+}
+
+// Gather `bytes` bytes from every rank (setup only).
+int allgather_bytes(noor_moe_handle* h, const void* mine, void* all, size_t bytes) {
+  DevBuf t;
+  CKR(t.ensure(bytes * (h->G + 1)));
+  CK(cudaMemcpy(t.p, mine, bytes, cudaMemcpyHostToDevice));
+  CKN(noor::nccl().AllGather(t.p, t.as<uint8_t>() + bytes, bytes, ncclUint8, h->comm, h->own));
+  CKR(setup_sync(h));
+  CK(cudaMemcpy(all, t.as<uint8_t>() + bytes, bytes * h->G, cudaMemcpyDeviceToHost));
+  return NOOR_MOE_OK;
+}
+
+void peer_release(noor_moe_handle* h) {
+  for (void* p : h->ipc_opened) cudaIpcCloseMemHandle(p);
+  h->ipc_opened.clear();
+  DevBuf* bufs[] = {&h->pxrecv, &h->py, &h->psync, &h->pseq, &h->pstatus, &h->dest_base, &h->grp_orank,
+                    &h->grp_oshift};
+  for (DevBuf* b : bufs) b->release();
+  h->peer = false;
+}
+
+// Choose the exchange and map every rank's buffers.  Collective: every rank
+// of the communicator calls it from noor_moe_create, and all take the same
+// decision.  Peer memory is used when the layer is BF16, every pair of the
+// ranks' GPUs has peer access, every mapping opens and the variable
+// NOOR_MOE_EP_TRANSPORT is not "nccl"; otherwise the layer exchanges rows
+// through NCCL.  The peer buffers hold capP tokens per rank, capP the
+// largest max_tokens over the ranks.
+int peer_setup(noor_moe_handle* h) {
+  namespace P = noor::peer;
+  const int G = h->G, me = h->rank, E = h->E, k = h->k, d = h->d;
+  const char* env = std::getenv("NOOR_MOE_EP_TRANSPORT");
+  const bool want = h->bf16 && G <= P::kMaxRanks && E <= 128 && !(env && std::strcmp(env, "nccl") == 0);
+  struct Info {
+    int64_t pid, want, max_tokens;
+    char bus[40];
+  };
+  Info mine{};
+  mine.pid = (int64_t)getpid();
+  mine.want = want ? 1 : 0;
+  mine.max_tokens = std::max<int64_t>(h->desc.max_tokens, 128);
+  CK(cudaDeviceGetPCIBusId(mine.bus, sizeof(mine.bus), h->dev));
+  std::vector<Info> all(G);
+  CKR(allgather_bytes(h, &mine, all.data(), sizeof(Info)));
+  int64_t ok = want ? 1 : 0;
+  std::vector<int> ord(G, -1);
+  int64_t capP = 0;
+  for (int r = 0; r < G; ++r) {
+    capP = std::max(capP, all[r].max_tokens);
+    if (!all[r].want) ok = 0;
+    all[r].bus[sizeof(all[r].bus) - 1] = 0;
+    if (cudaDeviceGetByPCIBusId(&ord[r], all[r].bus) != cudaSuccess) {
+      cudaGetLastError();
+      ok = 0;
+      continue;
+    }
+    if (r != me) {
+      int can = 0;
+      if (cudaDeviceCanAccessPeer(&can, h->dev, ord[r]) != cudaSuccess || !can) ok = 0;
+    }
+  }
+  cudaGetLastError();
+  CKR(allreduce_min(h, &ok));
+  if (!ok) return NOOR_MOE_OK;
+
+  // this rank's buffers, cleared before any rank can see them
+  capP = round_up(capP, 128);
+  const int64_t cap_rows = (int64_t)G * capP * k;
+  if (cap_rows > INT32_MAX) return fail(NOOR_MOE_ERR_INVALID, "expert-parallel capacity overflows");
+  int rc = NOOR_MOE_OK;
+  auto alloc = [&]() -> int {
+    CKR(h->pxrecv.ensure(cap_rows * d * 2));
+    CKR(h->py.ensure(capP * k * d * 2));
+    CKR(h->psync.ensure(round_up(P::kCountsOff + (int64_t)G * E * 8, 4096)));
+    CKR(h->pseq.ensure(8));
+    CKR(h->pstatus.ensure(4));
+    CKR(h->dest_base.ensure(E * 4));
+    CKR(h->grp_orank.ensure(E * 4));
+    CKR(h->grp_oshift.ensure(E * 4));
+    CKR(h->grp_row.ensure((E + 1) * 4));
+    CKR(h->grp_mtile.ensure((E + 1) * 4));
+    CKR(h->grp_widx.ensure((E + 1) * 4));
+    CKR(h->h.ensure(cap_rows * h->ff * 2));
+    CK(cudaMemset(h->psync.p, 0, h->psync.bytes));
+    CK(cudaMemset(h->pseq.p, 0, 8));
+    CK(cudaMemset(h->pstatus.p, 0, 4));
+    CK(cudaDeviceSynchronize());
+    return NOOR_MOE_OK;
+  };
+  rc = alloc();
+  int64_t ok2 = rc == NOOR_MOE_OK ? 1 : 0;
+  CKR(allreduce_min(h, &ok2));
+  if (!ok2) {
+    peer_release(h);
+    return rc != NOOR_MOE_OK ? rc : NOOR_MOE_OK;
+  }
+
+  // exchange the buffers' IPC handles (and raw addresses, for ranks that
+  // share this process) and map the other ranks' buffers
+  struct Handles {
+    cudaIpcMemHandle_t x, y, sy;
+    uint64_t px, py, ps;
+  };
+  Handles hm{};
+  int64_t ok3 = 1;
+  if (cudaIpcGetMemHandle(&hm.x, h->pxrecv.p) != cudaSuccess || cudaIpcGetMemHandle(&hm.y, h->py.p) != cudaSuccess ||
+      cudaIpcGetMemHandle(&hm.sy, h->psync.p) != cudaSuccess) {
+    cudaGetLastError();
+    ok3 = 0;
+  }
+  hm.px = reinterpret_cast<uint64_t>(h->pxrecv.p);
+  hm.py = reinterpret_cast<uint64_t>(h->py.p);
+  hm.ps = reinterpret_cast<uint64_t>(h->psync.p);
+  std::vector<Handles> hs(G);
+  CKR(allgather_bytes(h, &hm, hs.data(), sizeof(Handles)));
+  P::Peers peers{};
+  peers.G = G;
+  peers.me = me;
+  const char* tenv = std::getenv("NOOR_MOE_PEER_TIMEOUT_MS");
+  const int64_t tms = tenv ? std::max<int64_t>(1, std::atoll(tenv)) : 10000;
+  peers.timeout_ns = tms * 1000000LL;
+  for (int r = 0; r < G && ok3; ++r) {
+    void *px = nullptr, *py = nullptr, *ps = nullptr;
+    if (r == me || all[r].pid == mine.pid) {
+      if (r != me) {
+        cudaError_t e = cudaDeviceEnablePeerAccess(ord[r], 0);
+        if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) ok3 = 0;
+        cudaGetLastError();
+      }
+      px = reinterpret_cast<void*>(hs[r].px);
+      py = reinterpret_cast<void*>(hs[r].py);
+      ps = reinterpret_cast<void*>(hs[r].ps);
+    } else {
+      void* m[3] = {nullptr, nullptr, nullptr};
+      const cudaIpcMemHandle_t* src[3] = {&hs[r].x, &hs[r].y, &hs[r].sy};
+      for (int i = 0; i < 3; ++i) {
+        if (cudaIpcOpenMemHandle(&m[i], *src[i], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+          cudaGetLastError();
+          ok3 = 0;
+          break;
+        }
+        h->ipc_opened.push_back(m[i]);
+      }
+      px = m[0];
+      py = m[1];
+      ps = m[2];
+    }
+    peers.xrecv[r] = static_cast<uint8_t*>(px);
+    peers.sync[r] = static_cast<uint8_t*>(ps);
+    h->peer_y[r] = py;
+  }
+  CKR(allreduce_min(h, &ok3));
+  if (!ok3) {
+    peer_release(h);
+    return NOOR_MOE_OK;
+  }
+  h->peers = peers;
+  h->capP = capP;
+  h->cap_recv = std::max(h->cap_recv, cap_rows);
+  CKR(encode_kmajor(&h->tm_pxrecv, h->pxrecv.p, cap_rows, d, tc::BM));
+  CKR(encode_kmajor(&h->tm_h, h->h.p, h->cap_recv, h->ff, tc::BM));
+  h->peer = true;
+  // the NCCL path's staging buffers are not used
+  DevBuf* unused[] = {&h->xp, &h->y, &h->xrecv, &h->ysend, &h->cnt_recv};
+  for (DevBuf* b : unused) b->release();
+  return NOOR_MOE_OK;
+}
+
+// The layer step under expert parallelism over peer memory (BF16), without
+// host synchronization:
+//   router -> plan (counts to every rank, barrier, tables) -> permute (rows
+//   into the owners' receive buffers; beside it, on a second stream, the
+//   dense/shared up projections) -> barrier -> expert GEMM 1 -> expert
+//   GEMM 2 (outputs back to the senders) -> barrier -> dense down
+//   projection with the fused combine.
+// Every rank runs the plan and both barriers, with or without tokens.
+int run_forward_peer(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtensorMap* tmx, void* out,
+                     int64_t T) {
+  namespace P = noor::peer;
+  const int d = h->d, k = h->k, E = h->E;
+  const bool poison = T > h->capP;
+  int tpb = 0;
+  if (T > 0 && !poison) CKR(run_router(h, s, x, T, &tpb));
+  else CK(cudaMemsetAsync(h->counts64.p, 0, E * 8, s));
+  const int64_t cap_rows = (int64_t)h->G * h->capP * k;
+  P::PlanOut po{h->grp_row.as<int32_t>(), h->grp_mtile.as<int32_t>(), h->grp_widx.as<int32_t>(),
+                h->grp_orank.as<int32_t>(), h->grp_oshift.as<int32_t>(), h->dest_base.as<int32_t>(),
+                h->counts_glob.as<int64_t>(), h->pstatus.as<int>(), h->pseq.as<uint64_t>(), h->d_err};
+  CKR(launch(h, s, K_EP_PLAN, [&] {
+    P::plan_kernel<<<1, P::kPlanThreads, 0, s>>>(h->peers, h->counts64.as<int64_t>(), E, h->El, h->tile_m, cap_rows,
+                                                 poison ? 1 : 0, po);
+  }));
+  if (poison) {
+    // every rank skips this step; leave this rank's error word clear
+    CK(cudaEventRecord(h->ev_done, s));
+    CKR(wait_event_deadline(h, h->ev_done, 120.0));
+    CK(cudaMemset(h->d_err, 0, sizeof(int)));
+    return fail(NOOR_MOE_ERR_INVALID,
+                "%lld tokens exceed the %lld tokens per rank that the expert-parallel buffers hold (the largest "
+                "max_tokens given at creation); every rank skipped this step",
+                (long long)T, (long long)h->capP);
+  }
+  // The side branches (dense up projection, shared expert) need only x: they
+  // run on a second stream beside the permute, whose NVLink stores then
+  // overlap a tensor-core GEMM.
+  const GluFfn dense{K_DENSE_GEMM1, K_DENSE_GEMM2, tmx, x, T, h->dff, h->desc.dense_act == NOOR_ACT_SILU,
+                     &h->tm_dw1, &h->tm_dw2, &h->tm_dh, nullptr, nullptr, nullptr, h->dense_h.p};
+  const GluFfn shared{K_SHARED_GEMM1, K_SHARED_GEMM2, tmx, x, T, h->ff, true, &h->tm_sw1, &h->tm_sw2, &h->tm_sh,
+                      nullptr, nullptr, nullptr, h->shared_h.p};
+  const bool side = T > 0 && (h->has_dense || h->has_shared);
+  const bool fork = side && kForkSidePeer;
+  cudaStream_t ss = fork ? h->aux : s;
+  auto side_branches = [&]() -> int {
+    if (h->has_dense) CKR(glu_up(h, ss, dense));
+    if (h->has_shared) {
+      CKR(glu_up(h, ss, shared));
+      CKR(glu_down(h, ss, shared, h->shared_out.p, nullptr));
+    }
+    return NOOR_MOE_OK;
+  };
+  if (fork) {
+    CK(cudaEventRecord(h->ev_fork, s));
+    CK(cudaStreamWaitEvent(h->aux, h->ev_fork, 0));
+    CKR(side_branches());
+    CK(cudaEventRecord(h->ev_join, h->aux));
+  }
+  if (T > 0) {
+    CKR(launch(h, s, K_PERMUTE, [&] {
+      const int64_t blocks = (T + P::kPermuteWarps - 1) / P::kPermuteWarps;
+      const unsigned grid = (unsigned)(fork ? std::min<int64_t>(blocks, h->num_sms) : blocks);
+      P::permute_peer_kernel<<<grid, P::kPermuteWarps * 32, 0, s>>>(
+          static_cast<const uint8_t*>(x), d * 2, (int32_t)T, k, (int32_t)((T + tpb - 1) / tpb), tpb,
+          h->idx.as<int32_t>(), h->lrank.as<int32_t>(), h->blk_base.as<int32_t>(), h->seg_start.as<int32_t>(),
+          h->dest_base.as<int32_t>(), h->El, h->peers, h->pstatus.as<int>(), h->dst_row.as<int32_t>());
+    }));
+  }
+  if (side && !fork) CKR(side_branches());  // in line, while the other ranks' rows arrive
+  auto barrier = [&]() -> int {
+    return launch(h, s, K_EP_BARRIER, [&] {
+      P::barrier_kernel<<<1, 32, 0, s>>>(h->peers, h->pseq.as<uint64_t>(), h->pstatus.as<int>(), h->d_err);
+    });
+  };
+  CKR(barrier());
+  GroupTable gt;
+  gt.row_start = h->grp_row.as<int32_t>();
+  gt.mtile_start = h->grp_mtile.as<int32_t>();
+  gt.weight_idx = h->grp_widx.as<int32_t>();
+  gt.G = E;
+  gt.dense_rows = -1;
+  const int64_t max_mtiles = (cap_rows + h->tile_m - 1) / h->tile_m + E;
+  const PeerOut pout{h->grp_orank.as<int32_t>(), h->grp_oshift.as<int32_t>(), h->peer_y};
+  CKR(launch_gemm<tc::EPI_SWIGLU_BF16>(h, s, K_EXPERT_GEMM1, h->tm_pxrecv, h->tm_w1, gt, 2 * h->ff, d, h->h.p, h->ff,
+                                       max_mtiles));
+  CKR(launch_gemm<tc::EPI_STORE_BF16>(h, s, K_EXPERT_GEMM2, h->tm_h, h->tm_w2, gt, d, h->ff, nullptr, d, max_mtiles,
+                                      nullptr, &pout));
+  CKR(barrier());
+  if (T == 0) return NOOR_MOE_OK;
+  if (fork) CK(cudaStreamWaitEvent(s, h->ev_join, 0));
+  const float* shared_out = h->has_shared ? h->shared_out.as<float>() : nullptr;
+  if (h->has_dense) {
+    const CombineArgs comb{h->py.p, h->dst_row.as<int32_t>(), h->wts.as<float>(), shared_out, k};
+    return glu_down(h, s, dense, out, &comb);
+  }
+  return launch(h, s, K_COMBINE, [&] {
+    const unsigned grid = (unsigned)((T + dispatch::kCombineWarps - 1) / dispatch::kCombineWarps);
+    dispatch::combine_kernel<bf16, bf16><<<grid, dispatch::kCombineWarps * 32, 0, s>>>(
+        h->py.as<bf16>(), h->dst_row.as<int32_t>(), h->wts.as<float>(), nullptr, shared_out, (int32_t)T, d, k,
+        (bf16*)out);
+  });
+}
+
 // ============================================================== forward
 
 // x, out: device pointers of the layer dtype.  tmx: tensor map of x (BF16).
@@ -719,6 +1059,7 @@ int ep_exchange(noor_moe_handle* h, cudaStream_t s, int kind, const EpPlan& plan
 // (and shared) up projections run on a second stream while the rows cross
 // NVLink; the dense down projection waits for the returned expert rows.
 int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtensorMap* tmx, void* out, int64_t T) {
+  if (h->peer) return run_forward_peer(h, s, x, tmx, out, T);
   const int d = h->d, k = h->k, E = h->E;
   const int64_t b = h->bf16 ? 2 : 4;
   const GluFfn dense{K_DENSE_GEMM1, K_DENSE_GEMM2, tmx, x, T, h->dff, h->desc.dense_act == NOOR_ACT_SILU,
@@ -727,10 +1068,14 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
   const GluFfn shared{K_SHARED_GEMM1, K_SHARED_GEMM2, tmx, x, T, h->ff, true, &h->tm_sw1, &h->tm_sw2, &h->tm_sh,
                       h->sg32.as<float>(), h->su32.as<float>(), h->sd32.as<float>(), h->shared_h.p};
   const bool fuse_combine = h->bf16 && h->has_dense;
-  const bool side = h->G > 1 && (h->has_dense || h->has_shared) && T > 0;
+  // The side branches (dense up projection, shared expert) run on a second
+  // stream under the NCCL exchange, from the start, beside the transfers.  On
+  // one GPU they run in line after the expert GEMMs unless kForkSideSingle.
+  const bool side = (h->has_dense || h->has_shared) && T > 0 && (h->G > 1 || kForkSideSingle);
+  const bool side_first = side && h->G > 1;
   cudaStream_t ss = side ? h->aux : s;  // stream of the side branches' up projections
 
-  if (side) {
+  if (side_first) {
     CK(cudaEventRecord(h->ev_fork, s));
     CK(cudaStreamWaitEvent(h->aux, h->ev_fork, 0));
   }
@@ -747,7 +1092,7 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
     if (side) CK(cudaEventRecord(h->ev_join, h->aux));
     return NOOR_MOE_OK;
   };
-  if (side) CKR(side_branches());
+  if (side_first) CKR(side_branches());
 
   int tpb = 0;
   if (T == 0) {
@@ -755,8 +1100,15 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
     CK(cudaMemsetAsync(h->counts64.p, 0, E * 8, s));
   } else {
     CKR(run_router(h, s, x, T, &tpb));
+    if (side && !side_first) {
+      CK(cudaEventRecord(h->ev_fork, s));
+      CK(cudaStreamWaitEvent(h->aux, h->ev_fork, 0));
+      CKR(side_branches());
+    }
     CKR(launch(h, s, K_PERMUTE, [&] {
-      const unsigned grid = (unsigned)((T + dispatch::kPermuteWarps - 1) / dispatch::kPermuteWarps);
+      // persistent beside the side branch's GEMM, else a block per 4 tokens
+      const int64_t blocks = (T + dispatch::kPermuteWarps - 1) / dispatch::kPermuteWarps;
+      const unsigned grid = (unsigned)(side ? std::min<int64_t>(blocks, h->num_sms) : blocks);
       dispatch::permute_rows_kernel<<<grid, dispatch::kPermuteWarps * 32, 0, s>>>(
           static_cast<const uint8_t*>(x), (int32_t)(d * b), (int32_t)T, k, (int32_t)((T + tpb - 1) / tpb), tpb,
           h->idx.as<int32_t>(),
@@ -809,7 +1161,7 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
   if (h->G > 1) CKR(ep_exchange(h, s, K_A2A_COMBINE, plan, h->y.p, h->ysend.p, true));
 
   if (side) CK(cudaStreamWaitEvent(s, h->ev_join, 0));
-  else CKR(side_branches());
+  else CKR(side_branches());  // nothing to do: no side branch or no tokens
   if (T == 0) return NOOR_MOE_OK;
   const float* shared_out = h->has_shared ? h->shared_out.as<float>() : nullptr;
   if (fuse_combine) {
@@ -833,6 +1185,10 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
 int global_counts(noor_moe_handle* h, cudaStream_t s, const int64_t** src) {
   if (h->G == 1) {
     *src = h->counts64.as<int64_t>();
+    return NOOR_MOE_OK;
+  }
+  if (h->peer) {  // summed by the plan kernel
+    *src = h->counts_glob.as<int64_t>();
     return NOOR_MOE_OK;
   }
   CKN(noor::nccl().AllReduce(h->counts64.p, h->counts_glob.p, h->E, ncclInt64, ncclSum, h->comm, s));
@@ -926,8 +1282,12 @@ int noor_moe_create(const noor_moe_desc* desc, void* nccl_comm, noor_moe_handle*
   }
   if (h->scan_done.ensure(sizeof(int)) != NOOR_MOE_OK || cudaMemset(h->scan_done.p, 0, sizeof(int)) != cudaSuccess)
     return bail(fail(NOOR_MOE_ERR_CUDA, "scan counter setup failed"));
-  const int rc = ensure_workspace(h, std::max<int64_t>(desc->max_tokens, 128));
+  int rc = ensure_workspace(h, std::max<int64_t>(desc->max_tokens, 128));
   if (rc != NOOR_MOE_OK) return bail(rc);
+  if (h->G > 1) {
+    rc = peer_setup(h);
+    if (rc != NOOR_MOE_OK) return bail(rc);
+  }
   *out = h;
   return NOOR_MOE_OK;
 }
@@ -1071,7 +1431,7 @@ static int forward_impl(noor_moe_handle* h, const void* x, void* out, int64_t T,
   if (host) {
     if (T > 0) CK(cudaMemcpyAsync(h->x_in.p, x, xbytes, cudaMemcpyHostToDevice, s));
     xd = h->x_in.p;
-  } else if (h->bf16 && !route_only && (h->has_dense || h->has_shared)) {
+  } else if (h->bf16 && !route_only && (h->has_dense || h->has_shared) && T > 0) {
     if (x != h->tm_user_ptr || T != h->tm_user_T) {
       CKR(encode_kmajor(&h->tm_user, x, T, h->d, tc::BM));
       h->tm_user_ptr = x;
@@ -1129,6 +1489,7 @@ void noor_moe_destroy(noor_moe_handle* h) {
   {
     DeviceGuard g(h->dev);
     cudaDeviceSynchronize();
+    peer_release(h);
     DevBuf* bufs[] = {&h->gate, &h->bias, &h->scales, &h->w1, &h->w2, &h->wg32, &h->wu32, &h->wd32, &h->dw1,
                       &h->dw2, &h->dg32, &h->du32, &h->dd32, &h->sw1, &h->sw2, &h->sg32, &h->su32, &h->sd32,
                       &h->x_in, &h->out_buf, &h->idx, &h->wts, &h->lrank, &h->dst_row, &h->blk_hist,
@@ -1253,6 +1614,12 @@ int noor_moe_profile_end(noor_moe_handle* h, char* names, float* total_ms, int32
 }
 
 int64_t noor_moe_launch_count(const noor_moe_handle* h) { return h ? h->launches : 0; }
+
+int noor_moe_ep_transport(const noor_moe_handle* h) {
+  if (!h) return -1;
+  if (h->G == 1) return NOOR_MOE_EP_NONE;
+  return h->peer ? NOOR_MOE_EP_PEER : NOOR_MOE_EP_NCCL;
+}
 
 }  // extern "C"
 

@@ -1,0 +1,287 @@
+// peer_ep.cuh -- expert-parallel exchange over NVLink peer memory.
+//
+// Under expert parallelism rank r owns experts [r*El, (r+1)*El).  Instead of
+// staging rows for an all-to-all, every rank maps the other ranks' receive
+// buffers into its address space (CUDA IPC) and the kernels move the rows
+// themselves:
+//   plan     each rank stores its per-expert pick counts into every rank's
+//            sync area, signals, waits for all ranks, then builds from the
+//            full count matrix (identical on every rank) its receive group
+//            table and the receive-row bases of its own picks;
+//   permute  writes each picked row once, straight into the owner's receive
+//            buffer (a local store or an NVLink store);
+//   barrier  every rank's rows have landed;
+//   GEMMs    the expert down projection's epilogue stores each output row
+//            straight back into the buffer of the rank that sent the row, at
+//            that rank's own pick-row number (the single-GPU row layout);
+//   barrier  every rank's outputs have landed; the combine gathers locally.
+// Nothing waits on the host, so a whole layer step can be recorded in a CUDA
+// graph.  Every wait is bounded; a rank that gives up writes an error code
+// and marks the exchange failed, and the kernels after it skip their stores.
+#pragma once
+
+#include "common.cuh"
+
+namespace noor {
+namespace peer {
+
+constexpr int kMaxRanks = 8;
+
+// Each rank's peer-visible sync area:
+//   bytes [0, 64)       uint64 flag[src]: last barrier number rank src reached
+//   bytes [256, ...)    int64 cnt_all[src][E]: rank src's picks per expert
+constexpr int kCountsOff = 256;
+
+constexpr int STATUS_OK = 0;
+constexpr int STATUS_PEER_INVALID = 1;  // a rank published an over-capacity batch
+constexpr int STATUS_OVERFLOW = 2;      // a rank would receive more rows than its buffer holds
+constexpr int STATUS_TIMEOUT = 3;       // a barrier gave up waiting
+
+struct Peers {
+  uint8_t* sync[kMaxRanks];   // every rank's sync area, as mapped in this process
+  uint8_t* xrecv[kMaxRanks];  // every rank's receive buffer (rows of row_bytes)
+  int32_t G;
+  int32_t me;
+  int64_t timeout_ns;         // bound of every wait on another rank
+};
+
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Barrier number `seq` across the ranks, run by one full warp: lane r signals
+// rank r (after a system-scope fence, so every store this rank made before
+// is visible to whoever sees the signal), then waits, bounded, until rank r
+// has signalled this rank.  Returns false on every lane if any wait gave up.
+__device__ bool barrier_warp(const Peers& P, uint64_t seq) {
+  const int lane = threadIdx.x & 31;
+  __threadfence_system();
+  if (lane < P.G) st_release_sys(reinterpret_cast<uint64_t*>(P.sync[lane]) + P.me, seq);
+  bool ok = true;
+  if (lane < P.G) {
+    const uint64_t* f = reinterpret_cast<const uint64_t*>(P.sync[P.me]) + lane;
+    const uint64_t t0 = global_ns();
+    while (ld_acquire_sys(f) < seq) {
+      if ((int64_t)(global_ns() - t0) > P.timeout_ns) {
+        ok = false;
+        break;
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
+struct PlanOut {
+  int32_t* grp_row;     // [E+1] receive group j = le*G + src: first row in xrecv
+  int32_t* grp_mtile;   // [E+1] first BM-row tile of group j
+  int32_t* grp_widx;    // [E]   local expert of group j
+  int32_t* grp_orank;   // [E]   rank that sent group j's rows (its outputs go back there)
+  int32_t* grp_oshift;  // [E]   output row on that rank minus the row in xrecv
+  int32_t* dest_base;   // [E]   first row, on expert e's owner, of this rank's picks of e
+  int64_t* counts_glob; // [E]   picks of expert e over all ranks
+  int* status;          // STATUS_*
+  uint64_t* seq;        // barrier counter of this rank
+  int* err;             // device error word
+};
+
+constexpr int kPlanThreads = 256;
+
+// One block.  counts: this rank's picks per expert (ignored when poison is
+// set: the rank publishes -1 so that every rank skips this step).
+// cap_rows: rows every rank's receive buffer holds (the same on all ranks).
+__global__ void __launch_bounds__(kPlanThreads) plan_kernel(Peers P, const int64_t* __restrict__ counts, int32_t E,
+                                                            int32_t El, int32_t BM, int64_t cap_rows, int32_t poison,
+                                                            PlanOut o) {
+  __shared__ int64_t s_cnt[kMaxRanks * 128];
+  __shared__ int32_t s_pre[kMaxRanks][129];  // s_pre[src][e] = sum of cnt[src][e' < e]
+  __shared__ int s_status;
+  const int G = P.G, me = P.me;
+  const int tid = threadIdx.x;
+  // 1. publish this rank's counts in every rank's sync area
+  for (int i = tid; i < G * E; i += blockDim.x) {
+    const int r = i / E, e = i - r * E;
+    const int64_t c = poison ? -1 : counts[e];
+    reinterpret_cast<int64_t*>(P.sync[r] + kCountsOff)[me * E + e] = c;
+  }
+  __threadfence_system();
+  __syncthreads();
+  // 2. barrier
+  if (tid < 32) {
+    const uint64_t seq = *o.seq + 1;
+    const bool ok = barrier_warp(P, seq);
+    if (tid == 0) {
+      *o.seq = seq;
+      s_status = ok ? STATUS_OK : STATUS_TIMEOUT;
+    }
+  }
+  __syncthreads();
+  int status = s_status;
+  // 3. read the full count matrix
+  if (status == STATUS_OK) {
+    const int64_t* all = reinterpret_cast<const int64_t*>(P.sync[me] + kCountsOff);
+    for (int i = tid; i < G * E; i += blockDim.x) s_cnt[i] = __ldcv(all + i);
+  }
+  __syncthreads();
+  if (status == STATUS_OK) {
+    if (tid < G) {
+      int32_t run = 0;
+      bool bad = false;
+      for (int e = 0; e < E; ++e) {
+        s_pre[tid][e] = run;
+        const int64_t c = s_cnt[tid * E + e];
+        bad |= c < 0;
+        run += c > 0 ? (int32_t)c : 0;
+      }
+      s_pre[tid][E] = run;
+      if (bad) atomicMax(&s_status, STATUS_PEER_INVALID);
+    }
+    __syncthreads();
+    // rows each rank would receive; every rank checks every rank, so all agree
+    if (tid < G && s_status == STATUS_OK) {
+      int64_t rows = 0;
+      for (int src = 0; src < G; ++src) rows += s_pre[src][(tid + 1) * El] - s_pre[src][tid * El];
+      if (rows > cap_rows) atomicMax(&s_status, STATUS_OVERFLOW);
+    }
+    __syncthreads();
+    status = s_status;
+  }
+  if (status != STATUS_OK) {
+    // an empty plan: the GEMMs find no tiles, the permute stores nothing
+    for (int j = tid; j <= E; j += blockDim.x) {
+      o.grp_row[j] = 0;
+      o.grp_mtile[j] = 0;
+      if (j < E) {
+        o.grp_widx[j] = 0;
+        o.grp_orank[j] = 0;
+        o.grp_oshift[j] = 0;
+        o.dest_base[j] = 0;
+        o.counts_glob[j] = 0;
+      }
+    }
+    if (tid == 0) {
+      *o.status = status;
+      atomicExch(o.err, status == STATUS_TIMEOUT ? DEV_TIMEOUT_PEER : DEV_PEER_PLAN);
+    }
+    return;
+  }
+  // 4. receive groups of this rank in (local expert, source rank) order, so
+  //    that the GEMMs, which walk the tiles in order, interleave rows that
+  //    return to other ranks with rows that stay here and keep NVLink busy
+  //    for the whole down projection
+  if (tid == 0) {
+    int32_t row = 0, tiles = 0;
+    for (int j = 0; j < E; ++j) {
+      const int le = j / G, src = j - le * G;
+      const int e = me * El + le;
+      const int32_t c = (int32_t)s_cnt[src * E + e];
+      o.grp_row[j] = row;
+      o.grp_mtile[j] = tiles;
+      o.grp_widx[j] = le;
+      o.grp_orank[j] = src;
+      o.grp_oshift[j] = s_pre[src][e] - row;  // rank src keeps its picks of e from row s_pre[src][e]
+      row += c;
+      tiles += (c + BM - 1) / BM;
+    }
+    o.grp_row[E] = row;
+    o.grp_mtile[E] = tiles;
+  }
+  // 5. where this rank's picks of each expert land on the expert's owner, and
+  //    the global utilization counts
+  for (int e = tid; e < E; e += blockDim.x) {
+    const int r = e / El;
+    int32_t base = 0;  // rows of the owner's groups before (le, me): experts r*El.. e-1 from every rank ...
+    int64_t tot = 0;
+    for (int src = 0; src < G; ++src) {
+      base += s_pre[src][e] - s_pre[src][r * El];
+      if (src < me) base += (int32_t)s_cnt[src * E + e];  // ... and expert e from ranks before this one
+      tot += s_cnt[src * E + e];
+    }
+    o.dest_base[e] = base;
+    o.counts_glob[e] = tot;
+  }
+  if (tid == 0) *o.status = STATUS_OK;
+}
+
+// A barrier as its own launch (one warp).  Skipped, on every rank alike, when
+// the step's plan failed.
+__global__ void __launch_bounds__(32) barrier_kernel(Peers P, uint64_t* seq, int* status, int* err) {
+  if (*status != STATUS_OK) return;
+  const uint64_t s = *seq + 1;
+  const bool ok = barrier_warp(P, s);
+  if (threadIdx.x == 0) {
+    *seq = s;
+    if (!ok) {
+      *status = STATUS_TIMEOUT;
+      atomicExch(err, DEV_TIMEOUT_PEER);
+    }
+  }
+}
+
+// Dispatch under expert parallelism: each warp reads a token's row once
+// (4 KB for d = 2048 in one batch of loads) and writes it to each pick's row
+// in the receive buffer of the expert's owner.  dst_row[t, slot] is the pick's
+// row in this rank's own (single-GPU) layout, where the owner returns the
+// expert's output row.  The grid is persistent and small (one 4-warp block
+// per SM, 48 registers a thread) so that it runs beside a tensor-core GEMM
+// that holds the rest of each SM and its NVLink stores overlap that GEMM.
+constexpr int kPermuteWarps = 4;
+
+__global__ void __launch_bounds__(kPermuteWarps * 32) permute_peer_kernel(
+    const uint8_t* __restrict__ x, int32_t row_bytes, int32_t T, int32_t k, int32_t nblk, int32_t tpb,
+    const int32_t* __restrict__ idx, const int32_t* __restrict__ lrank, const int32_t* __restrict__ blk_base,
+    const int32_t* __restrict__ seg_start, const int32_t* __restrict__ dest_base, int32_t El, Peers P,
+    const int* __restrict__ status, int32_t* __restrict__ dst_row) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool store = *status == STATUS_OK;
+  const int nvec = row_bytes >> 4;
+  constexpr int U = 8;
+  for (int32_t t = blockIdx.x * kPermuteWarps + warp; t < T; t += gridDim.x * kPermuteWarps) {
+    uint8_t* dst[8];
+    const int32_t* bb = blk_base + t / tpb;  // blk_base[e][block] is bb[e * nblk]
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      dst[i] = nullptr;
+      if (i < k) {
+        const int32_t e = __ldg(idx + (int64_t)t * k + i);
+        const int32_t local = __ldg(bb + (int64_t)e * nblk) + __ldg(lrank + (int64_t)t * k + i);
+        if (lane == 0) dst_row[(int64_t)t * k + i] = local;
+        const int32_t r = e / El;
+        const int32_t remote = __ldg(dest_base + e) + local - __ldg(seg_start + e);
+        dst[i] = P.xrecv[r] + (int64_t)remote * row_bytes;
+      }
+    }
+    if (!store) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)t * row_bytes);
+    for (int base = lane; base < nvec; base += 32 * U) {
+      uint4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (base + 32 * u < nvec) v[u] = __ldg(src + base + 32 * u);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i < k) {
+          uint4* d = reinterpret_cast<uint4*>(dst[i]);
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (base + 32 * u < nvec) d[base + 32 * u] = v[u];
+        }
+      }
+    }
+  }
+  __threadfence_system();  // the rows are visible on their owners before the next barrier signals
+}
+
+}  // namespace peer
+}  // namespace noor

@@ -77,7 +77,25 @@ struct Params {
   const float* wts;       // [T][k]
   const float* shared;    // [T][ldc] f32 shared-expert output, nullable
   int32_t k;
+  // Expert parallelism over peer memory (EPI_STORE_BF16): when out_rank is
+  // set, the output rows of group g go to rank out_rank[g]'s buffer
+  // out_peer[out_rank[g]] (mapped into this process) at row + out_shift[g],
+  // instead of to C.
+  const int32_t* out_rank;
+  const int32_t* out_shift;
+  void* out_peer[8];
 };
+
+// Output base and row shift of the tile's group.
+__device__ __forceinline__ void tile_output(const Params& p, int32_t g, void** C, int32_t* shift) {
+  if (p.out_rank) {
+    *C = p.out_peer[__ldg(p.out_rank + g)];
+    *shift = __ldg(p.out_shift + g);
+  } else {
+    *C = p.C;
+    *shift = 0;
+  }
+}
 
 // ---------------------------------------------------------------- PTX helpers
 
@@ -237,6 +255,34 @@ __device__ __forceinline__ void write_chunk32_staged(void* C, int64_t ldc, int r
   __syncwarp();  // the buffer is reused by the next chunk
 }
 
+// The same for a 32-row x 64-column chunk (lane i holds row row0 + i: p0 =
+// columns col..col+31, p1 = col+32..col+63) through a 4 KB buffer: 8
+// consecutive lanes store one row's 128 bytes, whole 128-byte lines, 4 rows
+// per instruction.  For rows that cross NVLink to another GPU whole lines
+// travel in fewer, fuller packets than 64-byte pieces.
+__device__ __forceinline__ void write_chunk64_staged(void* C, int64_t ldc, int row0, int rows_valid, int col,
+                                                     const uint32_t (&p0)[16], const uint32_t (&p1)[16],
+                                                     uint8_t* stage, int lane) {
+  const int sw = lane & 7;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    *reinterpret_cast<uint4*>(stage + lane * 128 + ((j ^ sw) << 4)) =
+        make_uint4(p0[4 * j], p0[4 * j + 1], p0[4 * j + 2], p0[4 * j + 3]);
+    *reinterpret_cast<uint4*>(stage + lane * 128 + (((j + 4) ^ sw) << 4)) =
+        make_uint4(p1[4 * j], p1[4 * j + 1], p1[4 * j + 2], p1[4 * j + 3]);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int piece = lane + 32 * j;
+    const int r = piece >> 3, part = piece & 7;
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + r * 128 + ((part ^ (r & 7)) << 4));
+    if (r < rows_valid)
+      *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(C) + (int64_t)(row0 + r) * ldc + col + part * 8) = v;
+  }
+  __syncwarp();  // the buffer is reused by the next chunk
+}
+
 template <int EPI>
 __device__ __forceinline__ void store_chunk32(void* C, int64_t ldc, int row, int col, const uint32_t (&v)[32],
                                               const uint32_t (&u)[32]) {
@@ -305,15 +351,19 @@ __device__ __forceinline__ void combine_chunk32(const Params& p, int row, int co
 
 // Epilogue of one accumulator tile, run by one epilogue warp: TMEM lanes
 // 32*q .. +31 (the tile's rows row0 + 32*q + lane), column half `part`.
-// With `stage` (2 KB of shared memory for this warp) BF16 outputs leave
-// through write_chunk32_staged; without it each thread stores its own row.
+// With `stage` (4 KB of shared memory for this warp) BF16 outputs leave
+// through write_chunk32_staged (write_chunk64_staged for the plain store);
+// without it each thread stores its own row.
+// Outputs go to rows + shift of C (the combine reads its inputs at the
+// unshifted rows).
 template <int BN, int EPI>
-__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t t_base, int32_t row0, int32_t rows, int32_t nt,
-                                              int q, int part, int lane, uint8_t* stage) {
+__device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t shift, uint32_t t_base, int32_t row0,
+                                              int32_t rows, int32_t nt, int q, int part, int lane, uint8_t* stage) {
   const int row_in_tile = q * 32 + lane;
   const bool valid = row_in_tile < rows;
   const int row = row0 + row_in_tile;
-  const int wrow0 = row0 + q * 32;
+  const int orow = row + shift;
+  const int wrow0 = row0 + q * 32 + shift;
   const int wrows = max(0, min(32, rows - q * 32));
   if constexpr (epi_gated(EPI)) {
     constexpr int HALF = BN / 2;
@@ -326,8 +376,8 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t t_base, 
       tmem_ld_wait();
       uint32_t pk[16];
       activate_chunk32<EPI>(g, u, pk);
-      if (stage) write_chunk32_staged(p.C, p.ldc, wrow0, wrows, nt * HALF + c, pk, stage, lane);
-      else if (valid) write_chunk32_direct(p.C, p.ldc, row, nt * HALF + c, pk);
+      if (stage) write_chunk32_staged(C, p.ldc, wrow0, wrows, nt * HALF + c, pk, stage, lane);
+      else if (valid) write_chunk32_direct(C, p.ldc, orow, nt * HALF + c, pk);
     }
   } else if constexpr (EPI == EPI_COMBINE_BF16) {
     constexpr int SPAN = BN / 2;
@@ -349,23 +399,39 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t t_base, 
       tmem_ld_wait();
       uint32_t pk[16];
       combine_chunk32(p, row, nt * BN + c, valid, g, dst, wv, pk);
-      if (stage) write_chunk32_staged(p.C, p.ldc, wrow0, wrows, nt * BN + c, pk, stage, lane);
-      else if (valid) write_chunk32_direct(p.C, p.ldc, row, nt * BN + c, pk);
+      if (stage) write_chunk32_staged(C, p.ldc, wrow0, wrows, nt * BN + c, pk, stage, lane);
+      else if (valid) write_chunk32_direct(C, p.ldc, orow, nt * BN + c, pk);
     }
   } else {
     constexpr int SPAN = BN / 2;
+    if constexpr (EPI == EPI_STORE_BF16) {
+      if (stage) {
+#pragma unroll 1
+        for (int c = part * SPAN; c < (part + 1) * SPAN; c += 64) {
+          uint32_t g0[32], g1[32];
+          tmem_ld32(t_base + c, g0);
+          tmem_ld32(t_base + c + 32, g1);
+          tmem_ld_wait();
+          uint32_t pk0[16], pk1[16];
+          activate_chunk32<EPI>(g0, g0, pk0);
+          activate_chunk32<EPI>(g1, g1, pk1);
+          write_chunk64_staged(C, p.ldc, wrow0, wrows, nt * BN + c, pk0, pk1, stage, lane);
+        }
+        return;
+      }
+    }
 #pragma unroll 1
     for (int c = part * SPAN; c < (part + 1) * SPAN; c += 32) {
       uint32_t g[32];
       tmem_ld32(t_base + c, g);
       tmem_ld_wait();
       if constexpr (EPI == EPI_STORE_F32) {
-        if (valid) store_chunk32<EPI>(p.C, p.ldc, row, nt * BN + c, g, g);
+        if (valid) store_chunk32<EPI>(C, p.ldc, orow, nt * BN + c, g, g);
       } else {
         uint32_t pk[16];
         activate_chunk32<EPI>(g, g, pk);
-        if (stage) write_chunk32_staged(p.C, p.ldc, wrow0, wrows, nt * BN + c, pk, stage, lane);
-        else if (valid) write_chunk32_direct(p.C, p.ldc, row, nt * BN + c, pk);
+        if (stage) write_chunk32_staged(C, p.ldc, wrow0, wrows, nt * BN + c, pk, stage, lane);
+        else if (valid) write_chunk32_direct(C, p.ldc, orow, nt * BN + c, pk);
       }
     }
   }
@@ -515,7 +581,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!mbar_wait(&accf_bar[acc], acc_phase, &abort_flag, p.err, DEV_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t t_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      epilogue_tile<BN, EPI>(p, t_base, tc.row0, tc.rows, tc.nt, q, part, lane, nullptr);
+      void* Ct;
+      int32_t shift;
+      tile_output(p, tc.g, &Ct, &shift);
+      epilogue_tile<BN, EPI>(p, Ct, shift, t_base, tc.row0, tc.rows, tc.nt, q, part, lane, nullptr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce_bar[acc]);
@@ -524,6 +593,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         acc_phase ^= 1u;
       }
     }
+    if (p.out_rank) __threadfence_system();  // peer stores land before the next barrier signals
   }
 
   __syncthreads();
@@ -557,7 +627,7 @@ struct Cfg2 {
   static constexpr int A_BYTES = 128 * BK * 2;  // this CTA's A half
   static constexpr int B_BYTES = 128 * BK * 2;  // this CTA's B half
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGE_OUT_BYTES = 2048;  // per epilogue warp, write_chunk32_staged
+  static constexpr int STAGE_OUT_BYTES = 4096;  // per epilogue warp: write_chunk32/64_staged
   static constexpr int SMEM_BYTES = STAGES2 * STAGE_BYTES + EPI_WARPS * STAGE_OUT_BYTES + 1024;
   static constexpr uint32_t TMEM_COLS = 512;  // two 256-column accumulators
   static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
@@ -767,8 +837,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       if (!mbar_wait(&accf_bar[acc], acc_phase, &abort_flag, p.err, DEV_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t t_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      epilogue_tile<BN, EPI>(p, t_base, tc.row0 + 128 * (int32_t)rank, tc.rows - 128 * (int32_t)rank, tc.nt, q,
-                             part, lane, smOut + (warp - 2) * C::STAGE_OUT_BYTES);
+      void* Ct;
+      int32_t shift;
+      tile_output(p, tc.g, &Ct, &shift);
+      epilogue_tile<BN, EPI>(p, Ct, shift, t_base, tc.row0 + 128 * (int32_t)rank, tc.rows - 128 * (int32_t)rank,
+                             tc.nt, q, part, lane, smOut + (warp - 2) * C::STAGE_OUT_BYTES);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -780,6 +853,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         acc_phase ^= 1u;
       }
     }
+    if (p.out_rank) __threadfence_system();  // peer stores land before the next barrier signals
   }
 
   __syncthreads();

@@ -28,7 +28,16 @@ def main():
     ap.add_argument("--config", default="edge")
     ap.add_argument("--tokens", type=int, default=3000)
     ap.add_argument("--uneven", action="store_true", help="rank r gets tokens * (r + 1) // N tokens (rank 0 may get 0)")
+    ap.add_argument("--transport", choices=("auto", "nccl", "peer"), default="auto",
+                    help="nccl: force the NCCL exchange; peer: require the peer-memory exchange")
+    ap.add_argument("--graph", action="store_true",
+                    help="also replay the forward (device mode) as a captured CUDA graph, twice")
+    ap.add_argument("--overflow", action="store_true",
+                    help="the last rank first sends a batch above the agreed capacity: every rank must "
+                         "report the skipped step, then the next step must be exact")
     args = ap.parse_args()
+    if args.transport == "nccl":
+        os.environ["NOOR_MOE_EP_TRANSPORT"] = "nccl"
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
@@ -53,11 +62,49 @@ def main():
     h = pkg.api.Handle(cfg.d_model, cfg.n_experts, cfg.top_k, cfg.expert_ff, cfg.dense_ff, dtype=cfg.dtype,
                        device=local, world_size=world, rank=rank, max_tokens=max(tokens_of(rank), 1), comm=comm)
     h.load_weights(w)
+    transport = h.ep_transport
     x = x_of(rank)
     xin = W.bf16_bits(x) if cfg.dtype == W.BF16 else x
+    overflow = None
+    if args.overflow:
+        # capacity = the largest max_tokens over the ranks, rounded up to 128
+        cap = -(-max(max(tokens_of(r), 1) for r in range(world)) // 128) * 128
+        big = W.make_tokens(cfg, seed_offset=99, tokens=cap + 1) if rank == world - 1 else x
+        bigin = W.bf16_bits(big) if cfg.dtype == W.BF16 else big
+        try:
+            h.forward_host(np.ascontiguousarray(bigin))
+            overflow = "no error"
+        except pkg.api.NoorMoEError as e:
+            overflow = "invalid" if e.code == 1 else f"code {e.code}"
     out, idx, wt, counts = h.forward_host(np.ascontiguousarray(xin))
     out2, idx2, _, counts2 = h.forward_host(np.ascontiguousarray(xin))  # second call reuses the plan buffers
     same_twice = bool(np.array_equal(out, out2) and np.array_equal(counts, counts2))
+    graph_ok = None
+    if args.graph:
+        n = xin.shape[0]
+        tdt = torch.int16 if cfg.dtype == W.BF16 else torch.float32
+        xd = torch.from_numpy(np.ascontiguousarray(xin).view(np.int16) if cfg.dtype == W.BF16 else xin).to(dev)
+        od = torch.zeros_like(xd)
+        cd = torch.zeros(cfg.n_experts, dtype=torch.int64, device=dev)
+        cs = torch.cuda.Stream(dev)
+        cs.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(cs):
+            h.forward_device(xd.data_ptr(), od.data_ptr(), n, cs.cuda_stream, counts_ptr=cd.data_ptr())
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cs):
+            h.forward_device(xd.data_ptr(), od.data_ptr(), n, cs.cuda_stream, counts_ptr=cd.data_ptr())
+        od.zero_()
+        oks = []
+        for _ in range(2):
+            g.replay()
+            torch.cuda.synchronize(dev)
+            h.sync()
+            got = od.cpu().numpy()
+            got = got.view(np.uint16) if cfg.dtype == W.BF16 else got
+            oks.append(bool(np.array_equal(got, out) and np.array_equal(cd.cpu().numpy(), counts)))
+        del g
+        graph_ok = all(oks)
     h.close()
     pkg.api.comm_destroy(comm)
 
@@ -65,8 +112,14 @@ def main():
     gathered = [None] * world
     dist.all_gather_object(gathered, (rank, out, idx, counts))
     ok = True
+    flags = [None] * world
+    dist.all_gather_object(flags, (transport, overflow, graph_ok))
     report = {"world": world, "config": args.config, "tokens": [tokens_of(r) for r in range(world)],
-              "same_twice": same_twice}
+              "same_twice": same_twice, "transport": [f[0] for f in flags]}
+    if args.overflow:
+        report["overflow"] = [f[1] for f in flags]
+    if args.graph:
+        report["graph"] = [f[2] for f in flags]
     if rank == 0:
         ref_h = pkg.api.Handle(cfg.d_model, cfg.n_experts, cfg.top_k, cfg.expert_ff, cfg.dense_ff, dtype=cfg.dtype,
                                device=local, max_tokens=max(1, max(tokens_of(r) for r in range(world))))
@@ -91,6 +144,12 @@ def main():
                 mismatches.append({"rank": r, "what": "counts", "got": c.tolist(), "want": total_counts.tolist()})
         ref_h.close()
         ok = not mismatches and same_twice
+        if args.transport == "peer" and any(f[0] != "peer" for f in flags):
+            ok = False
+        if args.overflow and any(f[1] != "invalid" for f in flags):
+            ok = False
+        if args.graph and not all(f[2] for f in flags):
+            ok = False
         report.update(ok=ok, mismatches=mismatches[:8])
         print(json.dumps(report), flush=True)
     okt = torch.tensor([1 if ok else 0], device=dev)

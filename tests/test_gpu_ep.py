@@ -1,6 +1,6 @@
 """Multi-GPU: expert-parallel forward equals the single-GPU forward bit for
-bit (tests/multigpu/ep_check.py under torchrun).  Skipped with fewer than two
-visible GPUs."""
+bit (tests/multigpu/ep_check.py under torchrun), through both exchanges
+(peer memory and NCCL).  Skipped with fewer than two visible GPUs."""
 import os
 import subprocess
 import sys
@@ -24,7 +24,14 @@ def _run(n, *extra):
     return subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
 
 
-@pytest.mark.parametrize("extra", [(), ("--uneven",), ("--config", "proxy_tiny", "--tokens", "777")])
+@pytest.mark.parametrize("extra", [
+    ("--transport", "peer", "--graph"),             # BF16: NVLink peer-memory exchange, eager + CUDA graph
+    ("--transport", "peer", "--uneven"),            # one rank with no tokens, the others ragged
+    ("--transport", "peer", "--overflow"),          # an over-capacity batch is refused on every rank, then exact
+    ("--transport", "nccl"),                        # the NCCL all-to-all-v exchange
+    ("--transport", "nccl", "--uneven"),
+    ("--config", "proxy_tiny", "--tokens", "777"),  # F32 layer (NCCL exchange)
+])
 def test_expert_parallel_matches_single_gpu(extra):
     n = min(_ngpu(), 8)
     if n < 2:
