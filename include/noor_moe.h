@@ -178,6 +178,32 @@ NOOR_MOE_API int noor_moe_ep_plan(const int64_t* counts_local, const int64_t* co
 #define NOOR_MOE_EP_PEER 2
 NOOR_MOE_API int noor_moe_ep_transport(const noor_moe_handle* h);
 
+/* ---- expert utilization and the SMEBU bias update on the device ---- */
+
+/* The handle accumulates, on the device, the layer's ExpertUtilization
+ * (moe.rs:25-65) over every noor_moe_forward since the last reset: counts[E]
+ * (picks per expert) and tokens, the global ones under expert parallelism
+ * (the same on every rank).  noor_moe_route does not record, as
+ * MoERouter::route does not.
+ * noor_moe_utilization copies them to the host (counts [E] and tokens, each
+ * nullable) after the work queued on `stream` (NULL = the handle's stream),
+ * and with reset != 0 clears them (ExpertUtilization::reset). */
+NOOR_MOE_API int noor_moe_utilization(noor_moe_handle* h, int64_t* counts, int64_t* tokens, int reset,
+                                      void* stream);
+/* One training step's bias refresh, on the device: fractions = counts /
+ * tokens (ExpertUtilization::fractions, model.rs:180-183), SMEBU::update
+ * (smebu.rs:36-48) on the handle's momentum, and apply_to_router
+ * (smebu.rs:56-61): the new biases go straight into the router bias the next
+ * forward reads; the utilization is reset.  Asynchronous on `stream` (NULL:
+ * the handle's stream, synchronous).  Under expert parallelism every rank
+ * calls it and all get the same biases. */
+NOOR_MOE_API int noor_moe_smebu_update(noor_moe_handle* h, float kappa, float beta, float lambda, void* stream);
+/* Read (get, nullable) and/or overwrite (set, nullable) the SMEBU momentum
+ * [E] (zeros at creation), e.g. for checkpoints.  Synchronous. */
+NOOR_MOE_API int noor_moe_smebu_momentum(noor_moe_handle* h, float* get, const float* set);
+/* Copy the router bias [E] the next forward will use to the host. */
+NOOR_MOE_API int noor_moe_get_bias(noor_moe_handle* h, float* bias);
+
 /* ---- measurement hooks (CUDA events on the launching stream) ---- */
 
 /* Begin recording a start/stop event pair around every kernel the handle

@@ -39,6 +39,7 @@ EXPORTED_SYMBOLS = (
     "noor_moe_comm_id_size", "noor_moe_comm_get_id", "noor_moe_comm_init_rank",
     "noor_moe_comm_destroy", "noor_moe_profile_begin", "noor_moe_profile_end",
     "noor_moe_launch_count", "noor_moe_ep_plan", "noor_moe_route_static", "noor_moe_ep_transport",
+    "noor_moe_utilization", "noor_moe_smebu_update", "noor_moe_smebu_momentum", "noor_moe_get_bias",
 )
 
 EP_TRANSPORTS = {0: "none", 1: "nccl", 2: "peer"}
@@ -98,6 +99,10 @@ def lib() -> ctypes.CDLL:
     L.noor_moe_launch_count.restype = ctypes.c_int64
     L.noor_moe_ep_transport.argtypes = [_vp]
     L.noor_moe_ep_transport.restype = ctypes.c_int
+    L.noor_moe_utilization.argtypes = [_vp, _vp, _vp, ctypes.c_int, _vp]
+    L.noor_moe_smebu_update.argtypes = [_vp, ctypes.c_float, ctypes.c_float, ctypes.c_float, _vp]
+    L.noor_moe_smebu_momentum.argtypes = [_vp, _vp, _vp]
+    L.noor_moe_get_bias.argtypes = [_vp, _vp]
     L.noor_moe_route_static.argtypes = [_vp, _vp, _vp, _vp, _i64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                         ctypes.c_int32, _vp, _vp, _vp, _vp]
     _lib = L
@@ -211,6 +216,28 @@ class Handle:
 
     def launch_count(self) -> int:
         return int(lib().noor_moe_launch_count(self._h))
+
+    def utilization(self, reset: bool = False, stream: int = 0):
+        """(counts [E] int64, tokens) recorded on the device since the last reset."""
+        counts = np.empty(self.desc.n_experts, np.int64)
+        tokens = ctypes.c_int64(0)
+        check(lib().noor_moe_utilization(self._h, _ptr(counts), ctypes.byref(tokens), int(reset), stream or None))
+        return counts, int(tokens.value)
+
+    def smebu_update(self, kappa: float, beta: float, lam: float, stream: int = 0) -> None:
+        """SMEBU::update + apply_to_router on the device from the recorded utilization."""
+        check(lib().noor_moe_smebu_update(self._h, kappa, beta, lam, stream or None))
+
+    def smebu_momentum(self, set_to: Optional[np.ndarray] = None) -> np.ndarray:
+        m = np.empty(self.desc.n_experts, np.float32)
+        src = None if set_to is None else np.ascontiguousarray(set_to, np.float32)
+        check(lib().noor_moe_smebu_momentum(self._h, _ptr(m), _ptr(src)))
+        return m
+
+    def get_bias(self) -> np.ndarray:
+        b = np.empty(self.desc.n_experts, np.float32)
+        check(lib().noor_moe_get_bias(self._h, _ptr(b)))
+        return b
 
     @property
     def ep_transport(self) -> str:

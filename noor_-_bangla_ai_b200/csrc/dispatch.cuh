@@ -40,10 +40,14 @@ __device__ __forceinline__ int warp_inclusive_scan(int v) {
 // Runs in one thread block of any multiple of 32 threads (s_warp: 32 ints,
 // s_seg: E+1 ints); hist is read through L2 (ld.cg), so a block may scan
 // histograms that other blocks of the same grid have just written.
+// util (nullable, [E+1]): the layer's utilization since its last reset,
+// ExpertUtilization::record (moe.rs:40-45) for the whole batch: util[e] +=
+// counts[e], util[E] += tokens (every token has exactly k picks).
 __device__ void scan_segments_block(const int32_t* __restrict__ hist, int32_t nblk, int32_t E, int32_t BM,
                                     int64_t* __restrict__ counts, int32_t* __restrict__ seg_start,
                                     int32_t* __restrict__ blk_base, int32_t* __restrict__ mtile_start,
-                                    int32_t* s_warp, int32_t* s_seg) {
+                                    int32_t* s_warp, int32_t* s_seg, int64_t* __restrict__ util = nullptr,
+                                    int32_t k = 1) {
   const int N = E * nblk;
   const int nt = blockDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = nt >> 5;
@@ -80,9 +84,11 @@ __device__ void scan_segments_block(const int32_t* __restrict__ hist, int32_t nb
       seg_start[e] = s_seg[e];
       mtile_start[e] = tiles;
       tiles += (c + BM - 1) / BM;
+      if (util) util[e] += c;
     }
     seg_start[E] = s_seg[E];
     mtile_start[E] = tiles;
+    if (util) util[E] += s_seg[E] / k;
   }
 }
 

@@ -41,6 +41,7 @@
 #include "prepack.cuh"
 #include "router.cuh"
 #include "simt_gemm.cuh"
+#include "smebu.cuh"
 #include "tc_gemm.cuh"
 
 using namespace noor;
@@ -148,12 +149,12 @@ static int encode_kmajor(CUtensorMap* m, const void* base, int64_t rows, int64_t
 enum KernelKind : int {
   K_ROUTER = 0, K_ROUTER_SCORES, K_ROUTER_TOPK, K_SCAN, K_PERMUTE, K_EXPERT_GEMM1, K_EXPERT_GEMM2,
   K_DENSE_GEMM1, K_DENSE_GEMM2, K_SHARED_GEMM1, K_SHARED_GEMM2, K_COMBINE, K_PREPACK, K_A2A_DISPATCH,
-  K_A2A_COMBINE, K_COUNT_EXCHANGE, K_MATMUL, K_EP_PLAN, K_EP_BARRIER, K_NUM
+  K_A2A_COMBINE, K_COUNT_EXCHANGE, K_MATMUL, K_EP_PLAN, K_EP_BARRIER, K_SMEBU, K_NUM
 };
 static const char* kKindNames[K_NUM] = {
     "router", "router_scores", "router_topk", "scan", "permute", "expert_gemm1", "expert_gemm2",
     "dense_gemm1", "dense_gemm2", "shared_gemm1", "shared_gemm2", "combine", "prepack",
-    "a2a_dispatch", "a2a_combine", "count_exchange", "matmul", "ep_plan", "ep_barrier"};
+    "a2a_dispatch", "a2a_combine", "count_exchange", "matmul", "ep_plan", "ep_barrier", "smebu"};
 
 // ============================================================== handle
 
@@ -179,6 +180,10 @@ struct noor_moe_handle {
   int bn2 = 256;  // n-tile of GEMMs whose N is d
   bool pair2 = false;  // tensor-core GEMMs run on SM pairs (cta_group::2, 256-row tiles)
   int tile_m = 128;    // rows per GEMM tile of the group tables
+
+  // utilization since the last reset (counts [E], then tokens) and the SMEBU
+  // momentum [E], on the device
+  DevBuf util, smebu_m;
 
   // workspaces
   int64_t capT = 0;
@@ -509,7 +514,7 @@ int launch_tc2(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& 
                const GroupTable& gt, int N, int K, void* C, int64_t ldc, int64_t max_tiles,
                const CombineArgs* comb = nullptr, const PeerOut* po = nullptr) {
   auto kern = tc::grouped_gemm_2cta_kernel<EPI>;
-  CKR(ensure_smem_limit(kern, tc::Cfg2::SMEM_BYTES));
+  CKR(ensure_smem_limit(kern, tc::Cfg2<EPI>::SMEM_BYTES));
   tc::Params p{};
   p.groups = gt;
   p.N = N;
@@ -528,7 +533,7 @@ int launch_tc2(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& 
   set_peer_out(p, po);
   const int64_t tiles = std::max<int64_t>(1, max_tiles * p.n_tiles);
   const int clusters = (int)std::min<int64_t>(h->num_sms / 2, tiles);
-  return launch(h, s, kind, [&] { kern<<<2 * clusters, tc::NUM_THREADS, tc::Cfg2::SMEM_BYTES, s>>>(tA, tB, p); });
+  return launch(h, s, kind, [&] { kern<<<2 * clusters, tc::NUM_THREADS, tc::Cfg2<EPI>::SMEM_BYTES, s>>>(tA, tB, p); });
 }
 
 // A tensor-core GEMM with the layer's tile shape: SM pairs with 256-row
@@ -627,12 +632,15 @@ int glu_down(noor_moe_handle* h, cudaStream_t s, const GluFfn& f, void* out, con
 
 // Launch K1 and the scan.  Fills idx, wts, lrank, blk_hist, counts64,
 // seg_start, blk_base, mtile_start.  Returns the token-block size in *tpb.
-int run_router(noor_moe_handle* h, cudaStream_t s, const void* x, int64_t T, int* tpb_out) {
+// record: add the batch's counts to the layer's utilization (the forward
+// on one GPU; under expert parallelism the global counts are added later).
+int run_router(noor_moe_handle* h, cudaStream_t s, const void* x, int64_t T, int* tpb_out, bool record = false) {
   router::RouterOut ro{h->idx.as<int32_t>(), h->wts.as<float>(), h->lrank.as<int32_t>(), h->blk_hist.as<int32_t>()};
   const int E = h->E, k = h->k, d = h->d;
   int tpb = 0;
   router::FusedScan fs{h->scan_done.as<int>(), h->counts64.as<int64_t>(), h->seg_start.as<int32_t>(),
-                       h->blk_base.as<int32_t>(), h->mtile_start.as<int32_t>(), h->tile_m};
+                       h->blk_base.as<int32_t>(), h->mtile_start.as<int32_t>(), h->tile_m,
+                       record ? h->util.as<int64_t>() : nullptr};
   if (h->bf16) {
     const int NF = h->Epad / 8;
     const int warps = router::route_warps(T, h->num_sms);
@@ -967,7 +975,8 @@ int run_forward_peer(noor_moe_handle* h, cudaStream_t s, const void* x, const CU
   const int64_t cap_rows = (int64_t)h->G * h->capP * k;
   P::PlanOut po{h->grp_row.as<int32_t>(), h->grp_mtile.as<int32_t>(), h->grp_widx.as<int32_t>(),
                 h->grp_orank.as<int32_t>(), h->grp_oshift.as<int32_t>(), h->dest_base.as<int32_t>(),
-                h->counts_glob.as<int64_t>(), h->pstatus.as<int>(), h->pseq.as<uint64_t>(), h->d_err};
+                h->counts_glob.as<int64_t>(), h->pstatus.as<int>(), h->pseq.as<uint64_t>(), h->d_err,
+                h->util.as<int64_t>(), k};
   CKR(launch(h, s, K_EP_PLAN, [&] {
     P::plan_kernel<<<1, P::kPlanThreads, 0, s>>>(h->peers, h->counts64.as<int64_t>(), E, h->El, h->tile_m, cap_rows,
                                                  poison ? 1 : 0, po);
@@ -1099,7 +1108,7 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
     // A rank with no tokens still takes part in the exchange with zero counts.
     CK(cudaMemsetAsync(h->counts64.p, 0, E * 8, s));
   } else {
-    CKR(run_router(h, s, x, T, &tpb));
+    CKR(run_router(h, s, x, T, &tpb, h->G == 1));
     if (side && !side_first) {
       CK(cudaEventRecord(h->ev_fork, s));
       CK(cudaStreamWaitEvent(h->aux, h->ev_fork, 0));
@@ -1131,6 +1140,11 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
     max_mtiles = (T * k + h->tile_m - 1) / h->tile_m + E;
   } else {
     CKR(ep_plan(h, s, plan));
+    // global counts: the API's expert_counts and the layer's utilization
+    CKN(noor::nccl().AllReduce(h->counts64.p, h->counts_glob.p, h->E, ncclInt64, ncclSum, h->comm, s));
+    CKR(launch(h, s, K_SCAN, [&] {
+      smebu::util_accumulate_kernel<<<1, 256, 0, s>>>(h->counts_glob.as<int64_t>(), E, k, h->util.as<int64_t>());
+    }));
     CKR(ep_exchange(h, s, K_A2A_DISPATCH, plan, h->xp.p, h->xrecv.p, false));
     gt.row_start = h->grp_row.as<int32_t>();
     gt.mtile_start = h->grp_mtile.as<int32_t>();
@@ -1187,11 +1201,7 @@ int global_counts(noor_moe_handle* h, cudaStream_t s, const int64_t** src) {
     *src = h->counts64.as<int64_t>();
     return NOOR_MOE_OK;
   }
-  if (h->peer) {  // summed by the plan kernel
-    *src = h->counts_glob.as<int64_t>();
-    return NOOR_MOE_OK;
-  }
-  CKN(noor::nccl().AllReduce(h->counts64.p, h->counts_glob.p, h->E, ncclInt64, ncclSum, h->comm, s));
+  (void)s;  // summed in the forward: by the plan kernel (peer memory) or an all-reduce (NCCL)
   *src = h->counts_glob.as<int64_t>();
   return NOOR_MOE_OK;
 }
@@ -1282,6 +1292,9 @@ int noor_moe_create(const noor_moe_desc* desc, void* nccl_comm, noor_moe_handle*
   }
   if (h->scan_done.ensure(sizeof(int)) != NOOR_MOE_OK || cudaMemset(h->scan_done.p, 0, sizeof(int)) != cudaSuccess)
     return bail(fail(NOOR_MOE_ERR_CUDA, "scan counter setup failed"));
+  if (h->util.ensure((h->E + 1) * 8) != NOOR_MOE_OK || cudaMemset(h->util.p, 0, (h->E + 1) * 8) != cudaSuccess ||
+      h->smebu_m.ensure(h->E * 4) != NOOR_MOE_OK || cudaMemset(h->smebu_m.p, 0, h->E * 4) != cudaSuccess)
+    return bail(fail(NOOR_MOE_ERR_CUDA, "utilization setup failed"));
   int rc = ensure_workspace(h, std::max<int64_t>(desc->max_tokens, 128));
   if (rc != NOOR_MOE_OK) return bail(rc);
   if (h->G > 1) {
@@ -1495,7 +1508,8 @@ void noor_moe_destroy(noor_moe_handle* h) {
                       &h->x_in, &h->out_buf, &h->idx, &h->wts, &h->lrank, &h->dst_row, &h->blk_hist,
                       &h->blk_base, &h->counts64, &h->counts_glob, &h->seg_start, &h->mtile_start, &h->scores,
                       &h->xp, &h->h, &h->y, &h->xrecv, &h->ysend, &h->dense_h, &h->dense_out, &h->shared_h,
-                      &h->shared_out, &h->grp_row, &h->grp_mtile, &h->grp_widx, &h->cnt_recv, &h->scan_done};
+                      &h->shared_out, &h->grp_row, &h->grp_mtile, &h->grp_widx, &h->cnt_recv, &h->scan_done,
+                      &h->util, &h->smebu_m};
     for (DevBuf* b : bufs) b->release();
     if (h->h_cnt) cudaFreeHost(h->h_cnt);
     if (h->h_grp) cudaFreeHost(h->h_grp);
@@ -1615,6 +1629,56 @@ int noor_moe_profile_end(noor_moe_handle* h, char* names, float* total_ms, int32
 
 int64_t noor_moe_launch_count(const noor_moe_handle* h) { return h ? h->launches : 0; }
 
+int noor_moe_utilization(noor_moe_handle* h, int64_t* counts, int64_t* tokens, int reset, void* stream) {
+  if (!h) return fail(NOOR_MOE_ERR_INVALID, "null handle");
+  DeviceGuard g(h->dev);
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->own;
+  std::vector<int64_t> tmp(h->E + 1);
+  CK(cudaMemcpyAsync(tmp.data(), h->util.p, (h->E + 1) * 8, cudaMemcpyDeviceToHost, s));
+  if (reset) CK(cudaMemsetAsync(h->util.p, 0, (h->E + 1) * 8, s));
+  CK(cudaEventRecord(h->ev_done, s));
+  CKR(wait_event_deadline(h, h->ev_done, 300.0));
+  if (counts) std::memcpy(counts, tmp.data(), h->E * 8);
+  if (tokens) *tokens = tmp[h->E];
+  return NOOR_MOE_OK;
+}
+
+int noor_moe_smebu_update(noor_moe_handle* h, float kappa, float beta, float lambda, void* stream) {
+  if (!h) return fail(NOOR_MOE_ERR_INVALID, "null handle");
+  if (!h->weights) return fail(NOOR_MOE_ERR_STATE, "smebu_update before load_weights");
+  if (!(kappa > 0.0f)) return fail(NOOR_MOE_ERR_INVALID, "kappa must be positive");
+  DeviceGuard g(h->dev);
+  const bool host = stream == nullptr;
+  cudaStream_t s = host ? h->own : static_cast<cudaStream_t>(stream);
+  CKR(launch(h, s, K_SMEBU, [&] {
+    smebu::smebu_update_kernel<<<1, std::max(32, (h->E + 31) / 32 * 32), 0, s>>>(
+        h->util.as<int64_t>(), h->smebu_m.as<float>(), h->bias.as<float>(), h->E, kappa, beta, lambda);
+  }));
+  if (host) {
+    CK(cudaEventRecord(h->ev_done, s));
+    CKR(wait_event_deadline(h, h->ev_done, 300.0));
+  }
+  return NOOR_MOE_OK;
+}
+
+int noor_moe_smebu_momentum(noor_moe_handle* h, float* get, const float* set) {
+  if (!h) return fail(NOOR_MOE_ERR_INVALID, "null handle");
+  DeviceGuard g(h->dev);
+  CK(cudaDeviceSynchronize());
+  if (get) CK(cudaMemcpy(get, h->smebu_m.p, h->E * 4, cudaMemcpyDeviceToHost));
+  if (set) CK(cudaMemcpy(h->smebu_m.p, set, h->E * 4, cudaMemcpyHostToDevice));
+  return NOOR_MOE_OK;
+}
+
+int noor_moe_get_bias(noor_moe_handle* h, float* bias) {
+  if (!h || !bias) return fail(NOOR_MOE_ERR_INVALID, "null argument");
+  if (!h->weights) return fail(NOOR_MOE_ERR_STATE, "get_bias before load_weights");
+  DeviceGuard g(h->dev);
+  CK(cudaDeviceSynchronize());
+  CK(cudaMemcpy(bias, h->bias.p, h->E * 4, cudaMemcpyDeviceToHost));
+  return NOOR_MOE_OK;
+}
+
 int noor_moe_ep_transport(const noor_moe_handle* h) {
   if (!h) return -1;
   if (h->G == 1) return NOOR_MOE_EP_NONE;
@@ -1705,7 +1769,7 @@ extern "C" int noor_moe_route_static(const void* x, const void* gate, const floa
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   router::RouterOut ro{idx, w, reinterpret_cast<int32_t*>(sb + off_lrank), reinterpret_cast<int32_t*>(sb + off_hist)};
   float* scores = reinterpret_cast<float*>(sb + off_scores);
-  const router::FusedScan nofs{nullptr, nullptr, nullptr, nullptr, nullptr, tc::BM};
+  const router::FusedScan nofs{nullptr, nullptr, nullptr, nullptr, nullptr, tc::BM, nullptr};
   if (dtype == NOOR_DTYPE_BF16) {
     // the same kernel as noor_moe_route, so the results are identical
     const bf16* xg = static_cast<const bf16*>(x);

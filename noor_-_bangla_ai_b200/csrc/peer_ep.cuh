@@ -94,6 +94,8 @@ struct PlanOut {
   int* status;          // STATUS_*
   uint64_t* seq;        // barrier counter of this rank
   int* err;             // device error word
+  int64_t* util;        // nullable: utilization accumulator [E+1] (global counts, tokens)
+  int32_t k;            // picks per token
 };
 
 constexpr int kPlanThreads = 256;
@@ -210,8 +212,16 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(Peers P, const int64
     }
     o.dest_base[e] = base;
     o.counts_glob[e] = tot;
+    if (o.util) o.util[e] += tot;
   }
-  if (tid == 0) *o.status = STATUS_OK;
+  if (tid == 0) {
+    if (o.util) {
+      int64_t picks = 0;
+      for (int src = 0; src < G; ++src) picks += s_pre[src][E];
+      o.util[E] += picks / o.k;  // every token has exactly k picks
+    }
+    *o.status = STATUS_OK;
+  }
 }
 
 // A barrier as its own launch (one warp).  Skipped, on every rank alike, when

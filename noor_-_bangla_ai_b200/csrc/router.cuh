@@ -107,6 +107,7 @@ struct FusedScan {
   int32_t* blk_base;
   int32_t* mtile_start;
   int32_t BM;
+  int64_t* util;           // nullable: utilization accumulator [E+1] (dispatch::scan_segments_block)
 };
 
 // BF16 router: one block of W warps per SM-sized share of the batch; warp w
@@ -317,7 +318,7 @@ __global__ void __launch_bounds__(32 * kRouteMaxWarps) route_bf16_kernel(
   if (!s_last) return;
   __threadfence();
   dispatch::scan_segments_block(out.blk_hist, gridDim.x, E, scan.BM, scan.counts, scan.seg_start, scan.blk_base,
-                                scan.mtile_start, s_warp, s_seg);
+                                scan.mtile_start, s_warp, s_seg, scan.util, k);
   if (threadIdx.x == 0) *scan.done = 0;
 }
 
@@ -430,7 +431,7 @@ __global__ void __launch_bounds__(kTopkTPB) topk_from_scores_kernel(const float*
   if (!s_last) return;
   __threadfence();
   dispatch::scan_segments_block(out.blk_hist, gridDim.x, E, scan.BM, scan.counts, scan.seg_start, scan.blk_base,
-                                scan.mtile_start, s_warp, s_seg);
+                                scan.mtile_start, s_warp, s_seg, scan.util, k);
   if (threadIdx.x == 0) *scan.done = 0;
 }
 

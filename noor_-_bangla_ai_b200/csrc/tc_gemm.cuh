@@ -392,6 +392,19 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
         wv[i] = __ldg(p.wts + (int64_t)row * p.k + i);
       }
     }
+    // Bring this warp's whole column range of the k gathered rows into L2
+    // before the chunk loop, so that each chunk's loads wait on L2, not DRAM.
+    if (valid) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i < p.k) {
+          const char* yrow = reinterpret_cast<const char*>(p.y + (int64_t)dst[i] * p.ldc + nt * BN + part * SPAN);
+#pragma unroll
+          for (int off = 0; off < SPAN * 2; off += 128)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(yrow + off));
+        }
+      }
+    }
 #pragma unroll 1
     for (int c = part * SPAN; c < (part + 1) * SPAN; c += 32) {
       uint32_t g[32];
@@ -623,11 +636,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 constexpr int BM2 = 256;
 constexpr int STAGES2 = 5;
 
+template <int EPI>
 struct Cfg2 {
   static constexpr int A_BYTES = 128 * BK * 2;  // this CTA's A half
   static constexpr int B_BYTES = 128 * BK * 2;  // this CTA's B half
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGE_OUT_BYTES = 4096;  // per epilogue warp: write_chunk32/64_staged
+  // per epilogue warp: 4 KB for write_chunk64_staged (plain store), else 2 KB
+  // for write_chunk32_staged (less shared memory leaves more L1 for the
+  // combine's gathers)
+  static constexpr int STAGE_OUT_BYTES = EPI == EPI_STORE_BF16 ? 4096 : 2048;
   static constexpr int SMEM_BYTES = STAGES2 * STAGE_BYTES + EPI_WARPS * STAGE_OUT_BYTES + 1024;
   static constexpr uint32_t TMEM_COLS = 512;  // two 256-column accumulators
   static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
@@ -696,7 +713,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     grouped_gemm_2cta_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                              const Params p) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
-  using C = Cfg2;
+  using C = Cfg2<EPI>;
   constexpr int BN = 256;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));

@@ -105,6 +105,13 @@ def main():
             oks.append(bool(np.array_equal(got, out) and np.array_equal(cd.cpu().numpy(), counts)))
         del g
         graph_ok = all(oks)
+    # one more step from a clean utilization, then the SMEBU update on the
+    # device: every rank must hold the global counts and the same new bias
+    h.utilization(reset=True)
+    h.forward_host(np.ascontiguousarray(xin))
+    util_c, util_t = h.utilization()
+    h.smebu_update(5.0, 0.9, 0.05)
+    bias_ep = h.get_bias()
     h.close()
     pkg.api.comm_destroy(comm)
 
@@ -113,7 +120,7 @@ def main():
     dist.all_gather_object(gathered, (rank, out, idx, counts))
     ok = True
     flags = [None] * world
-    dist.all_gather_object(flags, (transport, overflow, graph_ok))
+    dist.all_gather_object(flags, (transport, overflow, graph_ok, util_c, util_t, bias_ep))
     report = {"world": world, "config": args.config, "tokens": [tokens_of(r) for r in range(world)],
               "same_twice": same_twice, "transport": [f[0] for f in flags]}
     if args.overflow:
@@ -142,6 +149,16 @@ def main():
         for r, o, i, c in gathered:
             if not np.array_equal(c, total_counts):
                 mismatches.append({"rank": r, "what": "counts", "got": c.tolist(), "want": total_counts.tolist()})
+        # the single-GPU handle recorded every rank's batch once: the global step
+        ref_c, ref_t = ref_h.utilization()
+        ref_h.smebu_update(5.0, 0.9, 0.05)
+        ref_bias = ref_h.get_bias()
+        for r, f in enumerate(flags):
+            if not (np.array_equal(f[3], ref_c) and f[4] == ref_t):
+                mismatches.append({"rank": r, "what": "utilization", "got": [f[3].tolist(), f[4]],
+                                   "want": [ref_c.tolist(), ref_t]})
+            if not np.array_equal(f[5], ref_bias):
+                mismatches.append({"rank": r, "what": "smebu bias"})
         ref_h.close()
         ok = not mismatches and same_twice
         if args.transport == "peer" and any(f[0] != "peer" for f in flags):
