@@ -112,6 +112,42 @@ NOOR_MOE_API int noor_moe_set_bias(noor_moe_handle* h, const float* bias);
 NOOR_MOE_API int noor_moe_forward(noor_moe_handle* h, const void* x, void* out, int64_t T, int32_t* topk_idx,
                      float* topk_w, int64_t* expert_counts, void* stream);
 
+/* The MoE block's FFN sublayer with its sandwich norm (block.rs:87-90,
+ * norm.rs:31-60): out = x + rms_norm(F(rms_norm(x, w_pre) * depth_scale),
+ * w_post) * depth_scale, F the layer of noor_moe_forward; rms_norm as
+ * tensor.rs:462-490 (sum of squares and division in f64).  x is the
+ * residual stream h.  Same pointer, dtype, EP and optional-output rules as
+ * noor_moe_forward (the routing outputs describe F's input).  Needs
+ * noor_moe_set_sandwich first (NOOR_MOE_ERR_STATE otherwise). */
+NOOR_MOE_API int noor_moe_ffn_sublayer_forward(noor_moe_handle* h, const void* x, void* out, int64_t T,
+                                               int32_t* topk_idx, float* topk_w, int64_t* expert_counts,
+                                               void* stream);
+/* SandwichNorm's parameters: pre_norm.weight and post_norm.weight [d] (f32,
+ * host), eps (RMSNorm eps, f64) and depth_scale (1/sqrt(layer_idx + 1) in
+ * f32, norm.rs:44). */
+NOOR_MOE_API int noor_moe_set_sandwich(noor_moe_handle* h, const float* pre_w, const float* post_w, double eps,
+                                       float depth_scale);
+
+/* Load MoE block `layer` of a Noor GGUF v3 checkpoint (gguf.rs:153-233, the
+ * tensor names of collect_model_tensors, gguf.rs:262-280) straight into the
+ * handle: blocks.<layer>.moe.router.{gate [d,E], biases [E], scales [E]},
+ * .moe.experts.<e>.{w_gate, w_up [d,ff], w_down [ff,d]} for this rank's
+ * experts only, .moe.shared.* (has_shared) and .dense.{w_gate, w_up [d,dff],
+ * w_down [dff,d]} (has_dense), F32 or F16 on disk, then the same device
+ * prepack as noor_moe_load_weights.  With norm_eps >= 0 it also loads
+ * .ffn_norm.{pre,post}.weight [d] and calls noor_moe_set_sandwich with that
+ * eps and depth_scale = 1/sqrt(layer + 1).  A missing tensor, a wrong shape
+ * or a malformed file returns NOOR_MOE_ERR_INVALID naming it. */
+NOOR_MOE_API int noor_moe_load_gguf(noor_moe_handle* h, const char* path, int32_t layer, double norm_eps);
+/* Host only: dims (up to 8), n_dims and dtype (0 F32, 1 F16) of one tensor
+ * of a GGUF file; NOOR_MOE_ERR_INVALID if the file is malformed or has no
+ * such tensor. */
+NOOR_MOE_API int noor_gguf_tensor_info(const char* path, const char* name, int64_t* dims, int32_t* n_dims,
+                                       int32_t* dtype);
+/* Host only: one tensor of a GGUF file as f32 (F16 converted exactly), n its
+ * element count. */
+NOOR_MOE_API int noor_gguf_read_f32(const char* path, const char* name, float* out, int64_t n);
+
 /* Router only: the batched form of MoERouter::route (moe.rs:79-107) plus the
  * utilization histogram.  Same pointer and dtype rules as noor_moe_forward;
  * idx and w are required, counts may be NULL. */

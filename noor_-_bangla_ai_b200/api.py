@@ -40,6 +40,8 @@ EXPORTED_SYMBOLS = (
     "noor_moe_comm_destroy", "noor_moe_profile_begin", "noor_moe_profile_end",
     "noor_moe_launch_count", "noor_moe_ep_plan", "noor_moe_route_static", "noor_moe_ep_transport",
     "noor_moe_utilization", "noor_moe_smebu_update", "noor_moe_smebu_momentum", "noor_moe_get_bias",
+    "noor_moe_ffn_sublayer_forward", "noor_moe_set_sandwich", "noor_moe_load_gguf", "noor_gguf_tensor_info",
+    "noor_gguf_read_f32",
 )
 
 EP_TRANSPORTS = {0: "none", 1: "nccl", 2: "peer"}
@@ -103,6 +105,11 @@ def lib() -> ctypes.CDLL:
     L.noor_moe_smebu_update.argtypes = [_vp, ctypes.c_float, ctypes.c_float, ctypes.c_float, _vp]
     L.noor_moe_smebu_momentum.argtypes = [_vp, _vp, _vp]
     L.noor_moe_get_bias.argtypes = [_vp, _vp]
+    L.noor_moe_ffn_sublayer_forward.argtypes = [_vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp]
+    L.noor_moe_set_sandwich.argtypes = [_vp, _vp, _vp, ctypes.c_double, ctypes.c_float]
+    L.noor_moe_load_gguf.argtypes = [_vp, ctypes.c_char_p, ctypes.c_int32, ctypes.c_double]
+    L.noor_gguf_tensor_info.argtypes = [ctypes.c_char_p, ctypes.c_char_p, _vp, _vp, _vp]
+    L.noor_gguf_read_f32.argtypes = [ctypes.c_char_p, ctypes.c_char_p, _vp, _i64]
     L.noor_moe_route_static.argtypes = [_vp, _vp, _vp, _vp, _i64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                         ctypes.c_int32, _vp, _vp, _vp, _vp]
     _lib = L
@@ -123,6 +130,24 @@ def _fptr(a: Optional[np.ndarray]):
 
 def _ptr(a: Optional[np.ndarray]):
     return None if a is None else ctypes.c_void_p(a.ctypes.data)
+
+
+def gguf_tensor_info(path: str, name: str):
+    """(dims, dtype) of one tensor of a GGUF file, parsed by the library (host only)."""
+    dims = np.zeros(8, np.int64)
+    nd = ctypes.c_int32(0)
+    dt = ctypes.c_int32(0)
+    check(lib().noor_gguf_tensor_info(os.fsencode(path), name.encode(), _ptr(dims), ctypes.byref(nd),
+                                      ctypes.byref(dt)))
+    return [int(v) for v in dims[:nd.value]], int(dt.value)
+
+
+def gguf_read_f32(path: str, name: str) -> np.ndarray:
+    """One tensor of a GGUF file as f32, read by the library (host only)."""
+    dims, _ = gguf_tensor_info(path, name)
+    out = np.empty(int(np.prod(dims)) if dims else 1, np.float32)
+    check(lib().noor_gguf_read_f32(os.fsencode(path), name.encode(), _ptr(out), out.size))
+    return out.reshape(dims)
 
 
 def matmul_f32(a: np.ndarray, b: np.ndarray) -> np.ndarray:
@@ -216,6 +241,31 @@ class Handle:
 
     def launch_count(self) -> int:
         return int(lib().noor_moe_launch_count(self._h))
+
+    def load_gguf(self, path: str, layer: int, norm_eps: float = -1.0) -> None:
+        """Load MoE block `layer` of a Noor GGUF checkpoint into the device
+        (and its sandwich norm when norm_eps >= 0)."""
+        check(lib().noor_moe_load_gguf(self._h, os.fsencode(path), int(layer), float(norm_eps)))
+
+    def set_sandwich(self, pre_w: np.ndarray, post_w: np.ndarray, eps: float, depth_scale: float) -> None:
+        pre = np.ascontiguousarray(pre_w, np.float32)
+        post = np.ascontiguousarray(post_w, np.float32)
+        check(lib().noor_moe_set_sandwich(self._h, _ptr(pre), _ptr(post), float(eps), float(depth_scale)))
+
+    def ffn_sublayer_host(self, x: np.ndarray, want_route: bool = True):
+        """out = x + post(F(pre(x))) (block.rs:87-90); host arrays in and out."""
+        T = x.shape[0]
+        out = np.empty_like(x)
+        idx = np.empty((T, self.k), np.int32) if want_route else None
+        wt = np.empty((T, self.k), np.float32) if want_route else None
+        counts = np.empty(self.desc.n_experts, np.int64)
+        check(lib().noor_moe_ffn_sublayer_forward(self._h, _ptr(x), _ptr(out), T, _ptr(idx), _ptr(wt),
+                                                  _ptr(counts), None))
+        return out, idx, wt, counts
+
+    def ffn_sublayer_device(self, x_ptr: int, out_ptr: int, T: int, stream: int, counts_ptr: int = 0) -> None:
+        check(lib().noor_moe_ffn_sublayer_forward(self._h, x_ptr, out_ptr, T, None, None, counts_ptr or None,
+                                                  stream))
 
     def utilization(self, reset: bool = False, stream: int = 0):
         """(counts [E] int64, tokens) recorded on the device since the last reset."""
@@ -477,6 +527,38 @@ class ParallelFFN:
 
     def param_count(self) -> int:
         return self.dense.param_count() + self.moe.param_count()
+
+
+class RMSNorm:
+    """norm.rs:3-28: x / sqrt(mean(x^2) + eps) * weight (weight ones at init)."""
+
+    def __init__(self, d_model: int, eps: float):
+        self.weight = np.ones(d_model, np.float32)
+        self.eps = float(eps)
+
+
+class SandwichNorm:
+    """norm.rs:31-60: pre/post RMSNorm around a sublayer, both scaled by
+    depth_scale = 1/sqrt(layer_idx + 1) (f32)."""
+
+    def __init__(self, d_model: int, eps: float, layer_idx: int):
+        self.pre_norm = RMSNorm(d_model, eps)
+        self.post_norm = RMSNorm(d_model, eps)
+        self.depth_scale = np.float32(1.0) / np.sqrt(np.float32(layer_idx + 1))
+
+
+def ffn_sublayer_forward(pffn: "ParallelFFN", norm: SandwichNorm, h: np.ndarray) -> np.ndarray:
+    """The FFN half of MoEBlock::forward (block.rs:87-90):
+    h + post(ParallelFFN(pre(h))), in one GPU call."""
+    moe = pffn.moe
+    x = np.asarray(h, np.float32)
+    if x.ndim != 2 or x.shape[1] != moe.d_model:
+        raise ValueError(f"expected h of shape (seq_len, {moe.d_model}), got {x.shape}")
+    dev = moe._device_handle()
+    dev.set_sandwich(norm.pre_norm.weight, norm.post_norm.weight, norm.pre_norm.eps, float(norm.depth_scale))
+    out, _idx, _wt, counts = dev.ffn_sublayer_host(moe._to_dtype(x))
+    moe.utilization.record_batch(counts, x.shape[0])
+    return moe._from_dtype(out)
 
 
 class SMEBU:

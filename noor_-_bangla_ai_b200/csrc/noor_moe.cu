@@ -24,7 +24,9 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
+#include <cmath>
 #include <cstring>
+#include <deque>
 #include <string>
 #include <mutex>
 #include <thread>
@@ -35,8 +37,10 @@
 #include "noor_moe.h"
 
 #include "common.cuh"
+#include "gguf.h"
 #include "dispatch.cuh"
 #include "nccl_dyn.h"
+#include "norm.cuh"
 #include "peer_ep.cuh"
 #include "prepack.cuh"
 #include "router.cuh"
@@ -149,12 +153,12 @@ static int encode_kmajor(CUtensorMap* m, const void* base, int64_t rows, int64_t
 enum KernelKind : int {
   K_ROUTER = 0, K_ROUTER_SCORES, K_ROUTER_TOPK, K_SCAN, K_PERMUTE, K_EXPERT_GEMM1, K_EXPERT_GEMM2,
   K_DENSE_GEMM1, K_DENSE_GEMM2, K_SHARED_GEMM1, K_SHARED_GEMM2, K_COMBINE, K_PREPACK, K_A2A_DISPATCH,
-  K_A2A_COMBINE, K_COUNT_EXCHANGE, K_MATMUL, K_EP_PLAN, K_EP_BARRIER, K_SMEBU, K_NUM
+  K_A2A_COMBINE, K_COUNT_EXCHANGE, K_MATMUL, K_EP_PLAN, K_EP_BARRIER, K_SMEBU, K_NORM_PRE, K_NORM_POST, K_NUM
 };
 static const char* kKindNames[K_NUM] = {
     "router", "router_scores", "router_topk", "scan", "permute", "expert_gemm1", "expert_gemm2",
     "dense_gemm1", "dense_gemm2", "shared_gemm1", "shared_gemm2", "combine", "prepack",
-    "a2a_dispatch", "a2a_combine", "count_exchange", "matmul", "ep_plan", "ep_barrier", "smebu"};
+    "a2a_dispatch", "a2a_combine", "count_exchange", "matmul", "ep_plan", "ep_barrier", "smebu", "norm_pre", "norm_post"};
 
 // ============================================================== handle
 
@@ -184,6 +188,14 @@ struct noor_moe_handle {
   // utilization since the last reset (counts [E], then tokens) and the SMEBU
   // momentum [E], on the device
   DevBuf util, smebu_m;
+
+  // sandwich norm of the FFN sublayer (noor_moe_ffn_sublayer_forward)
+  bool sandwich = false;
+  DevBuf pre_w, post_w;  // f32 [d]
+  double norm_eps = 0.0;
+  float depth_scale = 1.0f;
+  DevBuf xn, ffn;        // normalised input and ParallelFFN output, layer dtype [capT][d]
+  CUtensorMap tm_xn{};
 
   // workspaces
   int64_t capT = 0;
@@ -395,6 +407,11 @@ int ensure_workspace(noor_moe_handle* h, int64_t T) {
   if (h->has_shared) {
     CKR(h->shared_h.ensure(capT * h->ff * b));
     CKR(h->shared_out.ensure(capT * d * 4));
+  }
+  if (h->sandwich) {
+    CKR(h->xn.ensure(capT * d * b));
+    CKR(h->ffn.ensure(capT * d * b));
+    if (h->bf16) CKR(encode_kmajor(&h->tm_xn, h->xn.p, capT, d, tc::BM));
   }
   if (h->bf16) {
     if (!h->peer) CKR(encode_kmajor(&h->tm_xp, h->xp.p, Rl, d, tc::BM));
@@ -1417,8 +1434,35 @@ int noor_moe_set_bias(noor_moe_handle* h, const float* bias) {
   return NOOR_MOE_OK;
 }
 
+// Row-wise RMSNorm x sandwich depth scale (+ residual) over T rows of the
+// layer dtype.
+static int launch_norm(noor_moe_handle* h, cudaStream_t s, int kind, const void* x, const float* w,
+                       const void* resid, int64_t T, void* out) {
+  if (T == 0) return NOOR_MOE_OK;
+  const unsigned grid = (unsigned)((T + norm::kWarps - 1) / norm::kWarps);
+  return launch(h, s, kind, [&] {
+    if (h->bf16) {
+      if (resid)
+        norm::rms_norm_rows_kernel<bf16, true><<<grid, norm::kWarps * 32, 0, s>>>(
+            (const bf16*)x, w, h->norm_eps, h->depth_scale, (const bf16*)resid, (int32_t)T, h->d, (bf16*)out);
+      else
+        norm::rms_norm_rows_kernel<bf16, false><<<grid, norm::kWarps * 32, 0, s>>>(
+            (const bf16*)x, w, h->norm_eps, h->depth_scale, nullptr, (int32_t)T, h->d, (bf16*)out);
+    } else {
+      if (resid)
+        norm::rms_norm_rows_kernel<float, true><<<grid, norm::kWarps * 32, 0, s>>>(
+            (const float*)x, w, h->norm_eps, h->depth_scale, (const float*)resid, (int32_t)T, h->d, (float*)out);
+      else
+        norm::rms_norm_rows_kernel<float, false><<<grid, norm::kWarps * 32, 0, s>>>(
+            (const float*)x, w, h->norm_eps, h->depth_scale, nullptr, (int32_t)T, h->d, (float*)out);
+    }
+  });
+}
+
+// sublayer: the MoE block's FFN sublayer, out = x + post(layer(pre(x)))
+// (block.rs:87-90), instead of the layer alone.
 static int forward_impl(noor_moe_handle* h, const void* x, void* out, int64_t T, int32_t* topk_idx, float* topk_w,
-                        int64_t* expert_counts, void* stream, bool route_only) {
+                        int64_t* expert_counts, void* stream, bool route_only, bool sublayer = false) {
   if (!h) return fail(NOOR_MOE_ERR_INVALID, "null handle");
   if (!h->weights) return fail(NOOR_MOE_ERR_STATE, "forward before load_weights");
   if (h->comm_broken) return fail(NOOR_MOE_ERR_STATE, "communicator was aborted after a failed exchange");
@@ -1444,7 +1488,7 @@ static int forward_impl(noor_moe_handle* h, const void* x, void* out, int64_t T,
   if (host) {
     if (T > 0) CK(cudaMemcpyAsync(h->x_in.p, x, xbytes, cudaMemcpyHostToDevice, s));
     xd = h->x_in.p;
-  } else if (h->bf16 && !route_only && (h->has_dense || h->has_shared) && T > 0) {
+  } else if (h->bf16 && !route_only && !sublayer && (h->has_dense || h->has_shared) && T > 0) {
     if (x != h->tm_user_ptr || T != h->tm_user_T) {
       CKR(encode_kmajor(&h->tm_user, x, T, h->d, tc::BM));
       h->tm_user_ptr = x;
@@ -1457,7 +1501,13 @@ static int forward_impl(noor_moe_handle* h, const void* x, void* out, int64_t T,
     if (T > 0) CKR(run_router(h, s, xd, T, &tpb));
   } else {
     void* od = host ? h->out_buf.p : out;
-    CKR(run_forward(h, s, xd, tmx, od, T));
+    if (sublayer) {
+      CKR(launch_norm(h, s, K_NORM_PRE, xd, h->pre_w.as<float>(), nullptr, T, h->xn.p));
+      CKR(run_forward(h, s, h->xn.p, &h->tm_xn, h->ffn.p, T));
+      CKR(launch_norm(h, s, K_NORM_POST, h->ffn.p, h->post_w.as<float>(), xd, T, od));
+    } else {
+      CKR(run_forward(h, s, xd, tmx, od, T));
+    }
     if (host && T > 0) CK(cudaMemcpyAsync(out, od, xbytes, cudaMemcpyDeviceToHost, s));
   }
   const cudaMemcpyKind dk = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
@@ -1480,6 +1530,115 @@ static int forward_impl(noor_moe_handle* h, const void* x, void* out, int64_t T,
 int noor_moe_forward(noor_moe_handle* h, const void* x, void* out, int64_t T, int32_t* topk_idx, float* topk_w,
                      int64_t* expert_counts, void* stream) {
   return forward_impl(h, x, out, T, topk_idx, topk_w, expert_counts, stream, false);
+}
+
+int noor_moe_set_sandwich(noor_moe_handle* h, const float* pre_w, const float* post_w, double eps,
+                          float depth_scale) {
+  if (!h || !pre_w || !post_w) return fail(NOOR_MOE_ERR_INVALID, "null argument");
+  if (!(eps >= 0.0) || !(depth_scale > 0.0f)) return fail(NOOR_MOE_ERR_INVALID, "bad eps or depth_scale");
+  DeviceGuard g(h->dev);
+  CKR(h->pre_w.ensure(h->d * 4));
+  CKR(h->post_w.ensure(h->d * 4));
+  CK(cudaMemcpy(h->pre_w.p, pre_w, h->d * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(h->post_w.p, post_w, h->d * 4, cudaMemcpyHostToDevice));
+  h->norm_eps = eps;
+  h->depth_scale = depth_scale;
+  if (!h->sandwich) {
+    h->sandwich = true;
+    const int64_t b = h->bf16 ? 2 : 4;
+    CKR(h->xn.ensure(h->capT * h->d * b));
+    CKR(h->ffn.ensure(h->capT * h->d * b));
+    if (h->bf16) CKR(encode_kmajor(&h->tm_xn, h->xn.p, h->capT, h->d, tc::BM));
+  }
+  return NOOR_MOE_OK;
+}
+
+int noor_gguf_tensor_info(const char* path, const char* name, int64_t* dims, int32_t* n_dims, int32_t* dtype) {
+  if (!path || !name || !dims || !n_dims || !dtype) return fail(NOOR_MOE_ERR_INVALID, "null argument");
+  noor::gguf::File f;
+  if (!f.open(path)) return fail(NOOR_MOE_ERR_INVALID, "%s: %s", path, f.error().c_str());
+  const noor::gguf::TensorInfo* t = f.find(name);
+  if (!t) return fail(NOOR_MOE_ERR_INVALID, "%s: no tensor %s", path, name);
+  *n_dims = (int32_t)t->dims.size();
+  for (size_t i = 0; i < t->dims.size(); ++i) dims[i] = (int64_t)t->dims[i];
+  *dtype = (int32_t)t->type;
+  return NOOR_MOE_OK;
+}
+
+int noor_gguf_read_f32(const char* path, const char* name, float* out, int64_t n) {
+  if (!path || !name || !out) return fail(NOOR_MOE_ERR_INVALID, "null argument");
+  noor::gguf::File f;
+  if (!f.open(path)) return fail(NOOR_MOE_ERR_INVALID, "%s: %s", path, f.error().c_str());
+  const noor::gguf::TensorInfo* t = f.find(name);
+  if (!t) return fail(NOOR_MOE_ERR_INVALID, "%s: no tensor %s", path, name);
+  if ((uint64_t)n != t->numel) return fail(NOOR_MOE_ERR_INVALID, "tensor %s has %llu elements, not %lld", name,
+                                           (unsigned long long)t->numel, (long long)n);
+  std::vector<float> scratch;
+  std::memcpy(out, f.f32(*t, scratch), t->numel * 4);
+  return NOOR_MOE_OK;
+}
+
+int noor_moe_load_gguf(noor_moe_handle* h, const char* path, int32_t layer, double norm_eps) {
+  if (!h || !path || layer < 0) return fail(NOOR_MOE_ERR_INVALID, "bad argument");
+  noor::gguf::File f;
+  if (!f.open(path)) return fail(NOOR_MOE_ERR_INVALID, "%s: %s", path, f.error().c_str());
+  const std::string pre = "blocks." + std::to_string(layer) + ".";
+  std::deque<std::vector<float>> scratch;  // f32 copies of F16 tensors
+  auto get = [&](const std::string& name, std::initializer_list<uint64_t> shape, const float** out) -> int {
+    const noor::gguf::TensorInfo* t = f.find(name);
+    if (!t) return fail(NOOR_MOE_ERR_INVALID, "%s: no tensor %s", path, name.c_str());
+    if (t->dims != std::vector<uint64_t>(shape)) {
+      std::string want, got;
+      for (uint64_t v : shape) want += (want.empty() ? "" : ",") + std::to_string(v);
+      for (uint64_t v : t->dims) got += (got.empty() ? "" : ",") + std::to_string(v);
+      return fail(NOOR_MOE_ERR_INVALID, "%s: tensor %s has shape [%s], the layer needs [%s]", path, name.c_str(),
+                  got.c_str(), want.c_str());
+    }
+    scratch.emplace_back();
+    *out = f.f32(*t, scratch.back());
+    return NOOR_MOE_OK;
+  };
+  const uint64_t d = h->d, E = h->E, ff = h->ff, dff = h->dff;
+  const float *gate = nullptr, *bias = nullptr, *scales = nullptr;
+  CKR(get(pre + "moe.router.gate", {d, E}, &gate));
+  CKR(get(pre + "moe.router.biases", {E}, &bias));
+  CKR(get(pre + "moe.router.scales", {E}, &scales));
+  std::vector<const float*> wg(E, nullptr), wu(E, nullptr), wd(E, nullptr);
+  for (int e = h->e0; e < h->e0 + h->El; ++e) {  // this rank's experts only
+    const std::string ex = pre + "moe.experts." + std::to_string(e) + ".";
+    CKR(get(ex + "w_gate", {d, ff}, &wg[e]));
+    CKR(get(ex + "w_up", {d, ff}, &wu[e]));
+    CKR(get(ex + "w_down", {ff, d}, &wd[e]));
+  }
+  const float* shared[3] = {nullptr, nullptr, nullptr};
+  if (h->has_shared) {
+    CKR(get(pre + "moe.shared.w_gate", {d, ff}, &shared[0]));
+    CKR(get(pre + "moe.shared.w_up", {d, ff}, &shared[1]));
+    CKR(get(pre + "moe.shared.w_down", {ff, d}, &shared[2]));
+  }
+  const float* dense[3] = {nullptr, nullptr, nullptr};
+  if (h->has_dense) {
+    CKR(get(pre + "dense.w_gate", {d, dff}, &dense[0]));
+    CKR(get(pre + "dense.w_up", {d, dff}, &dense[1]));
+    CKR(get(pre + "dense.w_down", {dff, d}, &dense[2]));
+  }
+  const float *pre_w = nullptr, *post_w = nullptr;
+  if (norm_eps >= 0.0) {
+    CKR(get(pre + "ffn_norm.pre.weight", {d}, &pre_w));
+    CKR(get(pre + "ffn_norm.post.weight", {d}, &post_w));
+  }
+  CKR(noor_moe_load_weights(h, gate, bias, scales, wg.data(), wu.data(), wd.data(), shared, dense));
+  if (norm_eps >= 0.0) {
+    const float depth_scale = 1.0f / std::sqrt((float)(layer + 1));  // norm.rs:44
+    CKR(noor_moe_set_sandwich(h, pre_w, post_w, norm_eps, depth_scale));
+  }
+  return NOOR_MOE_OK;
+}
+
+int noor_moe_ffn_sublayer_forward(noor_moe_handle* h, const void* x, void* out, int64_t T, int32_t* topk_idx,
+                                  float* topk_w, int64_t* expert_counts, void* stream) {
+  if (h && !h->sandwich) return fail(NOOR_MOE_ERR_STATE, "ffn_sublayer_forward before set_sandwich");
+  return forward_impl(h, x, out, T, topk_idx, topk_w, expert_counts, stream, false, true);
 }
 
 int noor_moe_route(noor_moe_handle* h, const void* x, int64_t T, int32_t* idx, float* w, int64_t* counts,
@@ -1509,7 +1668,7 @@ void noor_moe_destroy(noor_moe_handle* h) {
                       &h->blk_base, &h->counts64, &h->counts_glob, &h->seg_start, &h->mtile_start, &h->scores,
                       &h->xp, &h->h, &h->y, &h->xrecv, &h->ysend, &h->dense_h, &h->dense_out, &h->shared_h,
                       &h->shared_out, &h->grp_row, &h->grp_mtile, &h->grp_widx, &h->cnt_recv, &h->scan_done,
-                      &h->util, &h->smebu_m};
+                      &h->util, &h->smebu_m, &h->pre_w, &h->post_w, &h->xn, &h->ffn};
     for (DevBuf* b : bufs) b->release();
     if (h->h_cnt) cudaFreeHost(h->h_cnt);
     if (h->h_grp) cudaFreeHost(h->h_grp);

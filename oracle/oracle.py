@@ -236,6 +236,24 @@ def rms_norm(a, weight, eps: float) -> np.ndarray:
     return out
 
 
+def ffn_sublayer_forward(w, x, top_k: int, pre_w, post_w, eps: float, depth_scale: float, bf16_storage: bool):
+    """The MoE block's FFN sublayer (block.rs:87-90): normed = rms_norm(h,
+    pre) * depth_scale (norm.rs:51-54); ffn = ParallelFFN(normed); out = h +
+    rms_norm(ffn, post) * depth_scale (norm.rs:57-60, tensor.rs:280-288).
+    With bf16_storage the normalised input is rounded to BF16, as a BF16
+    layer stores its input.  Returns out, idx, w, counts of the layer."""
+    x = _f32(x)
+    ds = np.float32(depth_scale)
+    xn = (rms_norm(x, pre_w, eps) * ds).astype(np.float32)
+    if bf16_storage:
+        u = xn.view(np.uint32).astype(np.uint64)
+        u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16  # RNE to BF16 (tensor.rs:23-28; finite values)
+        xn = (u.astype(np.uint32) << np.uint32(16)).view(np.float32)
+    ffn, idx, wt, counts = parallel_forward(w, xn, top_k)
+    out = (x + (rms_norm(ffn, post_w, eps) * ds).astype(np.float32)).astype(np.float32)
+    return out, idx, wt, counts, xn
+
+
 def smebu_update(momentum, biases, fractions, kappa: float, beta: float, lam: float):
     """SMEBU::update (smebu.rs:36-48), in place on momentum and biases."""
     assert momentum.dtype == np.float32 and biases.dtype == np.float32
