@@ -92,6 +92,64 @@ __device__ void scan_segments_block(const int32_t* __restrict__ hist, int32_t nb
   }
 }
 
+// The same scan with the histograms staged in shared memory (buf, buf_ints
+// ints): one coalesced read of the histograms and one coalesced write of the
+// bases, instead of strided L2 round trips per thread.  Falls back to
+// scan_segments_block when they do not fit.
+__device__ void scan_segments_block_staged(const int32_t* __restrict__ hist, int32_t nblk, int32_t E, int32_t BM,
+                                           int64_t* __restrict__ counts, int32_t* __restrict__ seg_start,
+                                           int32_t* __restrict__ blk_base, int32_t* __restrict__ mtile_start,
+                                           int32_t* s_warp, int32_t* s_seg, int64_t* __restrict__ util, int32_t k,
+                                           int32_t* buf, int32_t buf_ints) {
+  const int N = E * nblk;
+  if (N > buf_ints) {
+    scan_segments_block(hist, nblk, E, BM, counts, seg_start, blk_base, mtile_start, s_warp, s_seg, util, k);
+    return;
+  }
+  const int nt = blockDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = nt >> 5;
+  for (int i = threadIdx.x; i < N; i += nt) buf[i] = __ldcg(hist + i);
+  __syncthreads();
+  const int per = (N + nt - 1) / nt;
+  const int i0 = min(N, (int)threadIdx.x * per), i1 = min(N, i0 + per);
+  int sum = 0;
+  for (int i = i0; i < i1; ++i) sum += buf[i];
+  const int incl = warp_inclusive_scan(sum);
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int v = lane < nwarps ? s_warp[lane] : 0;
+    const int vi = warp_inclusive_scan(v);
+    if (lane < nwarps) s_warp[lane] = vi - v;
+    if (lane == nwarps - 1) s_seg[E] = vi;  // total picks
+  }
+  __syncthreads();
+  int run = s_warp[warp] + incl - sum;
+  for (int i = i0; i < i1; ++i) {  // in place: histogram -> exclusive bases
+    const int v = buf[i];
+    buf[i] = run;
+    run += v;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < N; i += nt) blk_base[i] = buf[i];
+  for (int e = threadIdx.x; e < E; e += nt) s_seg[e] = buf[e * nblk];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int tiles = 0;
+    for (int e = 0; e < E; ++e) {
+      const int c = s_seg[e + 1] - s_seg[e];
+      counts[e] = c;
+      seg_start[e] = s_seg[e];
+      mtile_start[e] = tiles;
+      tiles += (c + BM - 1) / BM;
+      if (util) util[e] += c;
+    }
+    seg_start[E] = s_seg[E];
+    mtile_start[E] = tiles;
+    if (util) util[E] += s_seg[E] / k;
+  }
+}
+
 __global__ void __launch_bounds__(kScanThreads) scan_segments_kernel(const int32_t* __restrict__ hist, int32_t nblk,
                                                                      int32_t E, int32_t BM,
                                                                      int64_t* __restrict__ counts,

@@ -44,6 +44,7 @@
 #include "peer_ep.cuh"
 #include "prepack.cuh"
 #include "router.cuh"
+#include "router_tc.cuh"
 #include "simt_gemm.cuh"
 #include "smebu.cuh"
 #include "tc_gemm.cuh"
@@ -181,6 +182,7 @@ struct noor_moe_handle {
   DevBuf sw1, sw2, sg32, su32, sd32;
   bool has_shared = false, has_dense = false;
   CUtensorMap tm_w1{}, tm_w2{}, tm_dw1{}, tm_dw2{}, tm_sw1{}, tm_sw2{};
+  CUtensorMap tm_gate{};  // BF16 router gate [Epad][d], box of roundup(E, 16) rows
   int bn2 = 256;  // n-tile of GEMMs whose N is d
   bool pair2 = false;  // tensor-core GEMMs run on SM pairs (cta_group::2, 256-row tiles)
   int tile_m = 128;    // rows per GEMM tile of the group tables
@@ -647,11 +649,37 @@ int glu_down(noor_moe_handle* h, cudaStream_t s, const GluFfn& f, void* out, con
 
 // ============================================================== router
 
+// The BF16 router (router_tc.cuh): one CTA per 128 tokens.  Shared by the
+// handle's router and noor_moe_route_static, so both give the same picks.
+int launch_route_tc(noor_moe_handle* h, cudaStream_t s, const CUtensorMap& tmx, const CUtensorMap& tmg,
+                    const float* bias, const float* scales, int64_t T, int d, int E, int k, const router::RouterOut& ro,
+                    const router::FusedScan& fs, int* err) {
+  const int npad = router::tc_npad(E);
+  const int smem = router::tc_smem_bytes(npad);
+  const unsigned grid = (unsigned)((T + router::kTcTPB - 1) / router::kTcTPB);
+  auto go = [&](auto kern) -> int {
+    CKR(ensure_smem_limit(kern, smem));
+    auto body = [&] { kern<<<grid, router::kTcThreads, smem, s>>>(tmx, tmg, bias, scales, (int32_t)T, d, E, k, ro, fs, err); };
+    if (h) return launch(h, s, K_ROUTER, body);
+    body();
+    CK(cudaGetLastError());
+    return NOOR_MOE_OK;
+  };
+  switch ((npad + 31) / 32) {
+    case 1: return go(router::route_tc_kernel<1>);
+    case 2: return go(router::route_tc_kernel<2>);
+    case 3: return go(router::route_tc_kernel<3>);
+    case 4: return go(router::route_tc_kernel<4>);
+    default: return fail(NOOR_MOE_ERR_UNSUPPORTED, "the tensor-core router supports at most 128 experts");
+  }
+}
+
 // Launch K1 and the scan.  Fills idx, wts, lrank, blk_hist, counts64,
 // seg_start, blk_base, mtile_start.  Returns the token-block size in *tpb.
 // record: add the batch's counts to the layer's utilization (the forward
 // on one GPU; under expert parallelism the global counts are added later).
-int run_router(noor_moe_handle* h, cudaStream_t s, const void* x, int64_t T, int* tpb_out, bool record = false) {
+int run_router(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtensorMap* tmx, int64_t T, int* tpb_out,
+               bool record = false) {
   router::RouterOut ro{h->idx.as<int32_t>(), h->wts.as<float>(), h->lrank.as<int32_t>(), h->blk_hist.as<int32_t>()};
   const int E = h->E, k = h->k, d = h->d;
   int tpb = 0;
@@ -659,34 +687,9 @@ int run_router(noor_moe_handle* h, cudaStream_t s, const void* x, int64_t T, int
                        h->blk_base.as<int32_t>(), h->mtile_start.as<int32_t>(), h->tile_m,
                        record ? h->util.as<int64_t>() : nullptr};
   if (h->bf16) {
-    const int NF = h->Epad / 8;
-    const int warps = router::route_warps(T, h->num_sms);
-    tpb = 16 * warps;
-    const int nblk = (int)((T + tpb - 1) / tpb);
-    const int kc_len = router::route_chunk(d, NF);
-    if (kc_len == 0) return fail(NOOR_MOE_ERR_UNSUPPORTED, "router gate slice does not fit shared memory");
-    const int smem = NF * 8 * (kc_len + 32) * 2;
-    const bf16* xg = reinterpret_cast<const bf16*>(x);
-    const bf16* gt = h->gate.as<bf16>();
-    const float* b = h->bias.as<float>();
-    const float* sc = h->scales.as<float>();
-#define NOOR_ROUTE_CASE(NF_)                                                                                 \
-  case NF_:                                                                                                  \
-    CKR(ensure_smem_limit(router::route_bf16_kernel<NF_>, smem));                                            \
-    CKR(launch(h, s, K_ROUTER, [&] {                                                                         \
-      router::route_bf16_kernel<NF_><<<nblk, 32 * warps, smem, s>>>(xg, gt, b, sc, (int32_t)T, d, E, k, kc_len, ro, \
-                                                                    fs);                                     \
-    }));                                                                                                     \
-    break;
-    switch (NF) {
-      NOOR_ROUTE_CASE(1) NOOR_ROUTE_CASE(2) NOOR_ROUTE_CASE(3) NOOR_ROUTE_CASE(4) NOOR_ROUTE_CASE(5)
-      NOOR_ROUTE_CASE(6) NOOR_ROUTE_CASE(7) NOOR_ROUTE_CASE(8) NOOR_ROUTE_CASE(9) NOOR_ROUTE_CASE(10)
-      NOOR_ROUTE_CASE(11) NOOR_ROUTE_CASE(12) NOOR_ROUTE_CASE(13) NOOR_ROUTE_CASE(14) NOOR_ROUTE_CASE(15)
-      NOOR_ROUTE_CASE(16)
-      default:
-        return fail(NOOR_MOE_ERR_UNSUPPORTED, "tensor-core router supports at most 128 experts");
-    }
-#undef NOOR_ROUTE_CASE
+    tpb = router::kTcTPB;
+    CKR(launch_route_tc(h, s, *tmx, h->tm_gate, h->bias.as<float>(), h->scales.as<float>(), T, d, E, k, ro, fs,
+                        h->d_err));
   } else {
     tpb = router::kTopkTPB;
     const int nblk = (int)((T + tpb - 1) / tpb);
@@ -987,7 +990,7 @@ int run_forward_peer(noor_moe_handle* h, cudaStream_t s, const void* x, const CU
   const int d = h->d, k = h->k, E = h->E;
   const bool poison = T > h->capP;
   int tpb = 0;
-  if (T > 0 && !poison) CKR(run_router(h, s, x, T, &tpb));
+  if (T > 0 && !poison) CKR(run_router(h, s, x, tmx, T, &tpb));
   else CK(cudaMemsetAsync(h->counts64.p, 0, E * 8, s));
   const int64_t cap_rows = (int64_t)h->G * h->capP * k;
   P::PlanOut po{h->grp_row.as<int32_t>(), h->grp_mtile.as<int32_t>(), h->grp_widx.as<int32_t>(),
@@ -1125,7 +1128,7 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
     // A rank with no tokens still takes part in the exchange with zero counts.
     CK(cudaMemsetAsync(h->counts64.p, 0, E * 8, s));
   } else {
-    CKR(run_router(h, s, x, T, &tpb, h->G == 1));
+    CKR(run_router(h, s, x, tmx, T, &tpb, h->G == 1));
     if (side && !side_first) {
       CK(cudaEventRecord(h->ev_fork, s));
       CK(cudaStreamWaitEvent(h->aux, h->ev_fork, 0));
@@ -1391,6 +1394,7 @@ int noor_moe_load_weights(noor_moe_handle* h, const float* gate, const float* bi
   CKR(h->gate.ensure((int64_t)h->Epad * d * 2));
   CK(cudaMemset(h->gate.p, 0, (int64_t)h->Epad * d * 2));
   CKR(pack(gate, d, E, h->gate.as<bf16>(), E, E, 0));
+  CKR(encode_kmajor(&h->tm_gate, h->gate.p, h->Epad, d, router::tc_npad(E)));
   // experts: W1 [El][2ff][d] with 128-row gate / up blocks interleaved; W2 [El][d][ff]
   CKR(h->w1.ensure((int64_t)El * 2 * ff * d * 2));
   CKR(h->w2.ensure((int64_t)El * d * ff * 2));
@@ -1488,7 +1492,7 @@ static int forward_impl(noor_moe_handle* h, const void* x, void* out, int64_t T,
   if (host) {
     if (T > 0) CK(cudaMemcpyAsync(h->x_in.p, x, xbytes, cudaMemcpyHostToDevice, s));
     xd = h->x_in.p;
-  } else if (h->bf16 && !route_only && !sublayer && (h->has_dense || h->has_shared) && T > 0) {
+  } else if (h->bf16 && !sublayer && T > 0) {
     if (x != h->tm_user_ptr || T != h->tm_user_T) {
       CKR(encode_kmajor(&h->tm_user, x, T, h->d, tc::BM));
       h->tm_user_ptr = x;
@@ -1498,7 +1502,7 @@ static int forward_impl(noor_moe_handle* h, const void* x, void* out, int64_t T,
   }
   if (route_only) {
     int tpb = 0;
-    if (T > 0) CKR(run_router(h, s, xd, T, &tpb));
+    if (T > 0) CKR(run_router(h, s, xd, tmx, T, &tpb));
   } else {
     void* od = host ? h->out_buf.p : out;
     if (sublayer) {
@@ -1898,14 +1902,7 @@ extern "C" int noor_moe_route_static(const void* x, const void* gate, const floa
   if (dtype == NOOR_DTYPE_F32 && E > 256) return fail(NOOR_MOE_ERR_UNSUPPORTED, "at most 256 experts");
   if (T > INT32_MAX / k) return fail(NOOR_MOE_ERR_INVALID, "too many tokens");
   const int Epad = (E + 7) / 8 * 8;
-  int nsm = 148;
-  {
-    int dev0 = 0;
-    CK(cudaGetDevice(&dev0));
-    CK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev0));
-  }
-  const int warps = router::route_warps(T, nsm);
-  const int tpb = dtype == NOOR_DTYPE_BF16 ? 16 * warps : router::kTopkTPB;
+  const int tpb = dtype == NOOR_DTYPE_BF16 ? router::kTcTPB : router::kTopkTPB;
   const int64_t nblk = (T + tpb - 1) / tpb;
   // carve the array: ranks | block histograms | block bases | segment starts | tile starts | [scores]
   const size_t off_lrank = 0;
@@ -1930,29 +1927,12 @@ extern "C" int noor_moe_route_static(const void* x, const void* gate, const floa
   float* scores = reinterpret_cast<float*>(sb + off_scores);
   const router::FusedScan nofs{nullptr, nullptr, nullptr, nullptr, nullptr, tc::BM, nullptr};
   if (dtype == NOOR_DTYPE_BF16) {
-    // the same kernel as noor_moe_route, so the results are identical
-    const bf16* xg = static_cast<const bf16*>(x);
-    const bf16* gt = static_cast<const bf16*>(gate);
-    const int NF = Epad / 8;
-    const int kc_len = router::route_chunk(d, NF);
-    if (kc_len == 0) return fail(NOOR_MOE_ERR_UNSUPPORTED, "router gate slice does not fit shared memory");
-    const int smem = NF * 8 * (kc_len + 32) * 2;
-#define NOOR_STATIC_ROUTE_CASE(NF_)                                                                            \
-  case NF_:                                                                                                    \
-    if (smem > 48 * 1024)                                                                                      \
-      CK(cudaFuncSetAttribute(router::route_bf16_kernel<NF_>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)); \
-    router::route_bf16_kernel<NF_><<<(unsigned)nblk, 32 * warps, smem, s>>>(xg, gt, bias, scales, (int32_t)T, d, E, \
-                                                                            k, kc_len, ro, nofs);                \
-    break;
-    switch (NF) {
-      NOOR_STATIC_ROUTE_CASE(1) NOOR_STATIC_ROUTE_CASE(2) NOOR_STATIC_ROUTE_CASE(3) NOOR_STATIC_ROUTE_CASE(4)
-      NOOR_STATIC_ROUTE_CASE(5) NOOR_STATIC_ROUTE_CASE(6) NOOR_STATIC_ROUTE_CASE(7) NOOR_STATIC_ROUTE_CASE(8)
-      NOOR_STATIC_ROUTE_CASE(9) NOOR_STATIC_ROUTE_CASE(10) NOOR_STATIC_ROUTE_CASE(11) NOOR_STATIC_ROUTE_CASE(12)
-      NOOR_STATIC_ROUTE_CASE(13) NOOR_STATIC_ROUTE_CASE(14) NOOR_STATIC_ROUTE_CASE(15) NOOR_STATIC_ROUTE_CASE(16)
-      default:
-        return fail(NOOR_MOE_ERR_UNSUPPORTED, "tensor-core router supports at most 128 experts");
-    }
-#undef NOOR_STATIC_ROUTE_CASE
+    // the same kernel as noor_moe_route, so the results are identical; the
+    // tensor maps are encoded on the host for this call (no allocation)
+    CUtensorMap tmx, tmg;
+    CKR(encode_kmajor(&tmx, x, T, d, router::kTcTPB));
+    CKR(encode_kmajor(&tmg, gate, Epad, d, router::tc_npad(E)));
+    CKR(launch_route_tc(nullptr, s, tmx, tmg, bias, scales, T, d, E, k, ro, nofs, nullptr));
   } else {
     const int64_t n = T * E;
     router::route_f32_scores_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(

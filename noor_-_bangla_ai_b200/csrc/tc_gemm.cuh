@@ -129,7 +129,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete.  Returns
-// false (after recording `code`) if the CTA is aborting or the limit passed.
+// false (after recording `code` in *err, when err is not null) if the CTA is
+// aborting or the limit passed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -139,7 +140,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (*abort_flag) return false;
     if (clock64() - start > kWaitLimitCycles) {
       *abort_flag = 1;
-      atomicCAS(err, 0, code);
+      if (err) atomicCAS(err, 0, code);
       return false;
     }
   }
