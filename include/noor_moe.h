@@ -192,6 +192,20 @@ NOOR_MOE_API int noor_moe_ep_plan(const int64_t* counts_local, const int64_t* co
                                   int64_t* send_rows, int64_t* send_off, int64_t* recv_rows, int64_t* recv_off,
                                   int32_t* grp_row, int32_t* grp_mtile, int32_t* grp_widx);
 
+/* Plan of rank `me` under the peer-memory exchange (the arithmetic the
+ * device runs inside noor_moe_forward, here on the host, e.g. to check it
+ * for any rank count): from the full count matrix cnt [G][E] (picks of
+ * expert e made on rank src), the receive group table of G*E/G = E groups in
+ * (local expert, source rank) order -- grp_row [E+1] (first row in the
+ * receive buffer), grp_mtile [E+1] (first BM-row tile), grp_widx [E] (local
+ * expert), grp_orank [E] (source rank), grp_oshift [E] (output row on the
+ * source minus the receive row) -- plus dest_base [E] (first receive row, on
+ * expert e's owner, of rank me's picks of e) and counts_glob [E].  Pure host
+ * arithmetic. */
+NOOR_MOE_API int noor_moe_peer_plan(const int64_t* cnt, int G, int E, int me, int BM, int32_t* grp_row,
+                                    int32_t* grp_mtile, int32_t* grp_widx, int32_t* grp_orank, int32_t* grp_oshift,
+                                    int32_t* dest_base, int64_t* counts_glob);
+
 /* How a handle's ranks exchange rows (no counterpart in the reference, which
  * runs on one device).  With world_size > 1, noor_moe_create is collective
  * and picks, the same on every rank:

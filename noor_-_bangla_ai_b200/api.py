@@ -41,7 +41,7 @@ EXPORTED_SYMBOLS = (
     "noor_moe_launch_count", "noor_moe_ep_plan", "noor_moe_route_static", "noor_moe_ep_transport",
     "noor_moe_utilization", "noor_moe_smebu_update", "noor_moe_smebu_momentum", "noor_moe_get_bias",
     "noor_moe_ffn_sublayer_forward", "noor_moe_set_sandwich", "noor_moe_load_gguf", "noor_gguf_tensor_info",
-    "noor_gguf_read_f32",
+    "noor_gguf_read_f32", "noor_moe_peer_plan",
 )
 
 EP_TRANSPORTS = {0: "none", 1: "nccl", 2: "peer"}
@@ -110,6 +110,7 @@ def lib() -> ctypes.CDLL:
     L.noor_moe_load_gguf.argtypes = [_vp, ctypes.c_char_p, ctypes.c_int32, ctypes.c_double]
     L.noor_gguf_tensor_info.argtypes = [ctypes.c_char_p, ctypes.c_char_p, _vp, _vp, _vp]
     L.noor_gguf_read_f32.argtypes = [ctypes.c_char_p, ctypes.c_char_p, _vp, _i64]
+    L.noor_moe_peer_plan.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int] + [_vp] * 7
     L.noor_moe_route_static.argtypes = [_vp, _vp, _vp, _vp, _i64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                         ctypes.c_int32, _vp, _vp, _vp, _vp]
     _lib = L
@@ -148,6 +149,20 @@ def gguf_read_f32(path: str, name: str) -> np.ndarray:
     out = np.empty(int(np.prod(dims)) if dims else 1, np.float32)
     check(lib().noor_gguf_read_f32(os.fsencode(path), name.encode(), _ptr(out), out.size))
     return out.reshape(dims)
+
+
+def peer_plan(cnt: np.ndarray, me: int, BM: int) -> dict:
+    """Rank `me`'s plan under the peer-memory exchange from the count matrix
+    cnt [G, E] -- the device's arithmetic, run on the host."""
+    cnt = np.ascontiguousarray(cnt, np.int64)
+    G, E = cnt.shape
+    out = {k: np.zeros(E + 1 if k in ("grp_row", "grp_mtile") else E, np.int32)
+           for k in ("grp_row", "grp_mtile", "grp_widx", "grp_orank", "grp_oshift", "dest_base")}
+    out["counts_glob"] = np.zeros(E, np.int64)
+    check(lib().noor_moe_peer_plan(_ptr(cnt), G, E, me, BM, _ptr(out["grp_row"]), _ptr(out["grp_mtile"]),
+                                   _ptr(out["grp_widx"]), _ptr(out["grp_orank"]), _ptr(out["grp_oshift"]),
+                                   _ptr(out["dest_base"]), _ptr(out["counts_glob"])))
+    return out
 
 
 def matmul_f32(a: np.ndarray, b: np.ndarray) -> np.ndarray:

@@ -238,6 +238,35 @@ struct noor_moe_handle {
   int64_t launches = 0;
 };
 
+extern "C" int noor_moe_peer_plan(const int64_t* cnt, int G, int E, int me, int BM, int32_t* grp_row,
+                                  int32_t* grp_mtile, int32_t* grp_widx, int32_t* grp_orank, int32_t* grp_oshift,
+                                  int32_t* dest_base, int64_t* counts_glob) {
+  if (!cnt || !grp_row || !grp_mtile || !grp_widx || !grp_orank || !grp_oshift || !dest_base || !counts_glob)
+    return fail(NOOR_MOE_ERR_INVALID, "null argument");
+  if (G < 1 || G > noor::peer::kMaxRanks || E <= 0 || E % G != 0 || me < 0 || me >= G || BM <= 0)
+    return fail(NOOR_MOE_ERR_INVALID, "bad plan arguments");
+  std::vector<int32_t> pre((size_t)G * (E + 1));
+  for (int src = 0; src < G; ++src) {
+    int64_t run = 0;
+    for (int e = 0; e < E; ++e) {
+      if (cnt[src * E + e] < 0) return fail(NOOR_MOE_ERR_INVALID, "negative count");
+      pre[(size_t)src * (E + 1) + e] = (int32_t)run;
+      run += cnt[src * E + e];
+    }
+    if (run > INT32_MAX) return fail(NOOR_MOE_ERR_INVALID, "count overflow");
+    pre[(size_t)src * (E + 1) + E] = (int32_t)run;
+  }
+  const noor::peer::PlanView pv{cnt, pre.data(), E + 1, G, E, E / G, me};
+  noor::peer::plan_recv_table(pv, BM, grp_row, grp_mtile, grp_widx, grp_orank, grp_oshift);
+  for (int e = 0; e < E; ++e) {
+    dest_base[e] = noor::peer::plan_dest_base(pv, e);
+    int64_t tot = 0;
+    for (int src = 0; src < G; ++src) tot += cnt[src * E + e];
+    counts_glob[e] = tot;
+  }
+  return NOOR_MOE_OK;
+}
+
 extern "C" int noor_moe_ep_plan(const int64_t* counts_local, const int64_t* counts_recv, int E, int G, int BM,
                                 int64_t* send_rows, int64_t* send_off, int64_t* recv_rows, int64_t* recv_off,
                                 int32_t* grp_row, int32_t* grp_mtile, int32_t* grp_widx) {

@@ -83,6 +83,63 @@ __device__ bool barrier_warp(const Peers& P, uint64_t seq) {
   return __all_sync(0xffffffffu, ok);
 }
 
+// ---- the plan's arithmetic, shared by plan_kernel and the host-side
+// noor_moe_peer_plan (so that it can be checked for any rank count on the
+// CPU).  cnt[src * E + e]: picks of expert e made on rank src; pre[src *
+// pre_ld + e]: sum of cnt[src][e' < e] (rank src keeps its picks of e from
+// row pre[src][e] of its own layout, the single-GPU one).
+
+struct PlanView {
+  const int64_t* cnt;
+  const int32_t* pre;
+  int32_t pre_ld;
+  int32_t G, E, El, me;
+};
+
+// Receive group j of this rank: (local expert le, source rank src) =
+// (j / G, j % G).  Ordering the groups expert-major interleaves rows that
+// return to other ranks with rows that stay here, so the GEMMs, which walk the
+// tiles in order, keep NVLink busy for the whole down projection.
+__host__ __device__ inline void plan_group(const PlanView& v, int j, int* src, int* le, int* e) {
+  *le = j / v.G;
+  *src = j - *le * v.G;
+  *e = v.me * v.El + *le;
+}
+
+// First row, on expert e's owner r, of this rank's picks of e: the rows of
+// the owner's groups before (le, me), i.e. experts r*El .. e-1 from every
+// rank, then expert e from the ranks before this one.
+__host__ __device__ inline int32_t plan_dest_base(const PlanView& v, int e) {
+  const int r = e / v.El;
+  int32_t base = 0;
+  for (int src = 0; src < v.G; ++src) {
+    base += v.pre[src * v.pre_ld + e] - v.pre[src * v.pre_ld + r * v.El];
+    if (src < v.me) base += (int32_t)v.cnt[src * v.E + e];
+  }
+  return base;
+}
+
+// The receive group table: first row, first BM-row tile, local expert,
+// source rank and output row shift of each group, [E+1] / [E] entries.
+__host__ __device__ inline void plan_recv_table(const PlanView& v, int BM, int32_t* grp_row, int32_t* grp_mtile,
+                                                int32_t* grp_widx, int32_t* grp_orank, int32_t* grp_oshift) {
+  int32_t row = 0, tiles = 0;
+  for (int j = 0; j < v.E; ++j) {
+    int src, le, e;
+    plan_group(v, j, &src, &le, &e);
+    const int32_t c = (int32_t)v.cnt[src * v.E + e];
+    grp_row[j] = row;
+    grp_mtile[j] = tiles;
+    grp_widx[j] = le;
+    grp_orank[j] = src;
+    grp_oshift[j] = v.pre[src * v.pre_ld + e] - row;  // back to row pre[src][e] on rank src
+    row += c;
+    tiles += (c + BM - 1) / BM;
+  }
+  grp_row[v.E] = row;
+  grp_mtile[v.E] = tiles;
+}
+
 struct PlanOut {
   int32_t* grp_row;     // [E+1] receive group j = le*G + src: first row in xrecv
   int32_t* grp_mtile;   // [E+1] first BM-row tile of group j
@@ -178,39 +235,15 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(Peers P, const int64
     }
     return;
   }
-  // 4. receive groups of this rank in (local expert, source rank) order, so
-  //    that the GEMMs, which walk the tiles in order, interleave rows that
-  //    return to other ranks with rows that stay here and keep NVLink busy
-  //    for the whole down projection
-  if (tid == 0) {
-    int32_t row = 0, tiles = 0;
-    for (int j = 0; j < E; ++j) {
-      const int le = j / G, src = j - le * G;
-      const int e = me * El + le;
-      const int32_t c = (int32_t)s_cnt[src * E + e];
-      o.grp_row[j] = row;
-      o.grp_mtile[j] = tiles;
-      o.grp_widx[j] = le;
-      o.grp_orank[j] = src;
-      o.grp_oshift[j] = s_pre[src][e] - row;  // rank src keeps its picks of e from row s_pre[src][e]
-      row += c;
-      tiles += (c + BM - 1) / BM;
-    }
-    o.grp_row[E] = row;
-    o.grp_mtile[E] = tiles;
-  }
+  // 4. receive groups of this rank (plan_group order)
+  const PlanView pv{s_cnt, &s_pre[0][0], 129, G, E, El, me};
+  if (tid == 0) plan_recv_table(pv, BM, o.grp_row, o.grp_mtile, o.grp_widx, o.grp_orank, o.grp_oshift);
   // 5. where this rank's picks of each expert land on the expert's owner, and
   //    the global utilization counts
   for (int e = tid; e < E; e += blockDim.x) {
-    const int r = e / El;
-    int32_t base = 0;  // rows of the owner's groups before (le, me): experts r*El.. e-1 from every rank ...
     int64_t tot = 0;
-    for (int src = 0; src < G; ++src) {
-      base += s_pre[src][e] - s_pre[src][r * El];
-      if (src < me) base += (int32_t)s_cnt[src * E + e];  // ... and expert e from ranks before this one
-      tot += s_cnt[src * E + e];
-    }
-    o.dest_base[e] = base;
+    for (int src = 0; src < G; ++src) tot += s_cnt[src * E + e];
+    o.dest_base[e] = plan_dest_base(pv, e);
     o.counts_glob[e] = tot;
     if (o.util) o.util[e] += tot;
   }
