@@ -39,6 +39,12 @@ PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_FLUSH_BYTES = 256 << 20
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one expert
+# GEMM 1 launch, from an ncu --set full capture of this kernel on the
+# Edge-like layer (16384 tokens, one B200): 537.4 MB read + 124.2 MB written,
+# against 671 MB algorithmic (x rows, W1 and h once).  Other workloads: None.
+GEMM1_DRAM_BYTES = {"edge": 661.6e6}
+
 
 def peaks():
     try:
@@ -309,16 +315,21 @@ def run_ours(args):
         launches = int(lt.item())
     value = T * world * args.steps / (tot_ms / 1e3)
 
-    # ---- end to end through the public API: pinned host in, pinned host out
-    e2e_steps = max(3, min(args.steps, 50))
+    # ---- end to end through the public API: pinned host in, pinned host out.
+    # Serial: each step uploads x, runs the forward and downloads out on one
+    # stream.  Pipelined (the reported value): two device buffers, and step
+    # i+1's upload and step i-1's download run on their own streams while
+    # step i's forward runs, as a serving loop would; every step still moves
+    # its own input up and its own output down inside the timed region.
+    e2e_serial_steps = max(3, min(args.steps, 20))
     for _ in range(2):
         x_dev.copy_(x_host, non_blocking=True)
         step()
         out_host.copy_(out_dev, non_blocking=True)
     barrier()
-    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_steps)]
-    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_steps)]
-    for i in range(e2e_steps):
+    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_serial_steps)]
+    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_serial_steps)]
+    for i in range(e2e_serial_steps):
         flush.zero_()
         e_s[i].record(stream)
         x_dev.copy_(x_host, non_blocking=True)
@@ -326,12 +337,67 @@ def run_ours(args):
         out_host.copy_(out_dev, non_blocking=True)
         e_e[i].record(stream)
     barrier()
-    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_s, e_e))
+    serial_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(e_s, e_e))
+
+    e2e_steps = max(4, min(args.steps, 100))
+    x_buf = [x_dev, torch.empty_like(x_dev)]
+    out_buf = [out_dev, torch.empty_like(out_dev)]
+    out_host_buf = [out_host, torch.empty_like(out_host).pin_memory()]
+    s_up, s_cmp, s_dn = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def fwd(b):
+        h.forward_device(x_buf[b].data_ptr(), out_buf[b].data_ptr(), T, s_cmp.cuda_stream,
+                         counts_ptr=counts.data_ptr())
+
+    s_cmp.wait_stream(stream)
+    pgraphs = None
+    if graph is not None:
+        pgraphs = []
+        for b in range(2):
+            with torch.cuda.stream(s_cmp):
+                fwd(b)
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s_cmp):
+                fwd(b)
+            pgraphs.append(g)
+    barrier()
+    ev_up = [torch.cuda.Event() for _ in range(e2e_steps)]
+    ev_cmp = [torch.cuda.Event() for _ in range(e2e_steps)]
+    ev_dn = [torch.cuda.Event() for _ in range(e2e_steps)]
+    p_start = torch.cuda.Event(enable_timing=True)
+    p_end = torch.cuda.Event(enable_timing=True)
+    p_start.record(s_up)
+    for i in range(e2e_steps):
+        b = i & 1
+        with torch.cuda.stream(s_up):
+            if i >= 2:
+                s_up.wait_event(ev_cmp[i - 2])  # the forward that read x_buf[b] is done
+            x_buf[b].copy_(x_host, non_blocking=True)
+            ev_up[i].record(s_up)
+        with torch.cuda.stream(s_cmp):
+            s_cmp.wait_event(ev_up[i])
+            if i >= 2:
+                s_cmp.wait_event(ev_dn[i - 2])  # out_buf[b] has been downloaded
+            if pgraphs is not None:
+                pgraphs[b].replay()
+            else:
+                fwd(b)
+            ev_cmp[i].record(s_cmp)
+        with torch.cuda.stream(s_dn):
+            s_dn.wait_event(ev_cmp[i])
+            out_host_buf[b].copy_(out_buf[b], non_blocking=True)
+            ev_dn[i].record(s_dn)
+    p_end.record(s_dn)
+    barrier()
+    e2e_ms = p_start.elapsed_time(p_end)
+    del pgraphs
     if world > 1:
-        tt = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        tt = torch.tensor([e2e_ms, serial_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_ms = float(tt.item())
+        e2e_ms, serial_ms = float(tt[0].item()), float(tt[1].item())
     e2e = T * world * e2e_steps / (e2e_ms / 1e3)
+    e2e_serial = T * world * e2e_serial_steps / (serial_ms / 1e3)
     io_bytes = int(x_host.numel() * x_host.element_size())
 
     # ---- roofline of each kernel from the live per-launch events
@@ -346,7 +412,9 @@ def run_ours(args):
         if dom:
             roof = {"bound": "tensor", "kernel": "expert_gemm1 (grouped SwiGLU gate/up, tcgen05)",
                     "achieved": dom["achieved"], "peak": dom["peak"], "unit": "TFLOP/s",
-                    "frac": dom["frac"], "traffic": None,
+                    "frac": dom["frac"],
+                    "traffic": GEMM1_DRAM_BYTES.get(cfg.name) if world == 1 else None,
+                    "traffic_unit": "bytes per launch (ncu capture)",
                     "peak_source": f"bf16_tflops_sustained, {pk_kind}",
                     "algorithmic_per_launch": dom["algorithmic_per_launch"],
                     "avg_launch_ms": dom["avg_ms"]}
@@ -357,7 +425,10 @@ def run_ours(args):
             "data": "synthetic (seeded Philox; x = RMSNorm(N(0,1)), weights N(0,0.02), bias U(-0.1,0.1))",
             "config": dict(config_dict(cfg, T, world, scaling), ep_transport=transport),
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes,
-                    "api": "noor_moe_forward (device mode) with pinned-host H2D/D2H in the timed region"},
+                    "api": "noor_moe_forward (device mode) with pinned-host H2D/D2H in the timed region",
+                    "mode": f"pipelined over {e2e_steps} steps: step i+1's H2D and step i-1's D2H on their own "
+                            "streams overlap step i's forward (two device buffers)",
+                    "serial_value": e2e_serial},
             "gpu_launches": launches,
             "timing": ("CUDA-graph replay of one forward per step; per-kernel times from an uncaptured pass"
                        if graph is not None else "plain calls; per-kernel events in the timed region"),

@@ -28,6 +28,38 @@ __device__ __forceinline__ int warp_inclusive_scan(int v) {
   return v;
 }
 
+// The per-expert tail of the scans below, with s_seg[0..E] holding the
+// segment starts (shared memory): counts, segment starts, the BM-row tile
+// starts (an exclusive warp scan) and the utilization, in parallel over the
+// experts -- no serial chain of global loads.  All threads call it.
+__device__ void finish_segments(int32_t E, int32_t BM, const int32_t* s_seg, int64_t* __restrict__ counts,
+                                int32_t* __restrict__ seg_start, int32_t* __restrict__ mtile_start,
+                                int64_t* __restrict__ util, int32_t k) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int c = s_seg[e + 1] - s_seg[e];
+    counts[e] = c;
+    seg_start[e] = s_seg[e];
+    if (util) util[e] += c;
+  }
+  if (warp == 0) {
+    int run = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const int c = e < E ? s_seg[e + 1] - s_seg[e] : 0;
+      const int t = (c + BM - 1) / BM;
+      const int incl = warp_inclusive_scan(t);
+      if (e < E) mtile_start[e] = run + incl - t;
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+      mtile_start[E] = run;
+      seg_start[E] = s_seg[E];
+      if (util) util[E] += s_seg[E] / k;
+    }
+  }
+}
+
 // From the per-token-block histograms, stored expert-major hist[E][nblk]:
 //   blk_base[e][b]  = first row of block b's picks of expert e
 //   seg_start[e]    = first row of expert e's segment, [E+1]
@@ -76,20 +108,7 @@ __device__ void scan_segments_block(const int32_t* __restrict__ hist, int32_t nb
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += nt) s_seg[e] = blk_base[(int64_t)e * nblk];
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int tiles = 0;
-    for (int e = 0; e < E; ++e) {
-      const int c = s_seg[e + 1] - s_seg[e];
-      counts[e] = c;
-      seg_start[e] = s_seg[e];
-      mtile_start[e] = tiles;
-      tiles += (c + BM - 1) / BM;
-      if (util) util[e] += c;
-    }
-    seg_start[E] = s_seg[E];
-    mtile_start[E] = tiles;
-    if (util) util[E] += s_seg[E] / k;
-  }
+  finish_segments(E, BM, s_seg, counts, seg_start, mtile_start, util, k);
 }
 
 // The same scan with the histograms staged in shared memory (buf, buf_ints
@@ -108,7 +127,17 @@ __device__ void scan_segments_block_staged(const int32_t* __restrict__ hist, int
   }
   const int nt = blockDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = nt >> 5;
-  for (int i = threadIdx.x; i < N; i += nt) buf[i] = __ldcg(hist + i);
+  {
+    constexpr int U = 8;  // eight independent L2 loads in flight per thread
+    for (int base = threadIdx.x; base < N; base += nt * U) {
+      int v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) v[u] = base + u * nt < N ? __ldcg(hist + base + u * nt) : 0;
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (base + u * nt < N) buf[base + u * nt] = v[u];
+    }
+  }
   __syncthreads();
   const int per = (N + nt - 1) / nt;
   const int i0 = min(N, (int)threadIdx.x * per), i1 = min(N, i0 + per);
@@ -134,20 +163,7 @@ __device__ void scan_segments_block_staged(const int32_t* __restrict__ hist, int
   for (int i = threadIdx.x; i < N; i += nt) blk_base[i] = buf[i];
   for (int e = threadIdx.x; e < E; e += nt) s_seg[e] = buf[e * nblk];
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int tiles = 0;
-    for (int e = 0; e < E; ++e) {
-      const int c = s_seg[e + 1] - s_seg[e];
-      counts[e] = c;
-      seg_start[e] = s_seg[e];
-      mtile_start[e] = tiles;
-      tiles += (c + BM - 1) / BM;
-      if (util) util[e] += c;
-    }
-    seg_start[E] = s_seg[E];
-    mtile_start[E] = tiles;
-    if (util) util[E] += s_seg[E] / k;
-  }
+  finish_segments(E, BM, s_seg, counts, seg_start, mtile_start, util, k);
 }
 
 __global__ void __launch_bounds__(kScanThreads) scan_segments_kernel(const int32_t* __restrict__ hist, int32_t nblk,

@@ -3,8 +3,8 @@
 // The router's dot products are a GEMM with a narrow N: scores[T, E] =
 // x[T, d] . gate_t[E, d]^T.  One CTA takes a tile of 128 tokens:
 //   warp 0 lane 0   TMA producer: per 64-column k-block, the x tile (128 rows,
-//                   16 KB) and the gate tile (NPAD rows) into a 4-stage ring
-//                   (128-byte swizzle)
+//                   16 KB) and the gate tile (NPAD rows) into a ring of up
+//                   to 8 stages (128-byte swizzle)
 //   warp 1 lane 0   MMA issuer: tcgen05.mma.cta_group::1.kind::f16, M = 128,
 //                   N = NPAD (E rounded up to 16), f32 accumulator in TMEM
 //   warps 2..5      epilogue: thread i owns token row i (TMEM lane i): it
@@ -25,13 +25,20 @@ namespace noor {
 namespace router {
 
 constexpr int kTcTPB = 128;       // tokens per CTA
-constexpr int kTcStages = 4;
+constexpr int kTcMaxStages = 8;
+constexpr int kTcRingBytes = 192 * 1024;  // stage ring budget: one CTA per SM
 constexpr int kTcThreads = 192;   // producer, MMA, 4 epilogue warps
 constexpr int kTcXBytes = kTcTPB * 64 * 2;  // one k-block of the x tile
 
 __host__ __device__ constexpr int tc_npad(int E) { return (E + 15) / 16 * 16; }
 __host__ __device__ constexpr int tc_stage_bytes(int npad) { return kTcXBytes + npad * 64 * 2; }
-__host__ constexpr int tc_smem_bytes(int npad) { return kTcStages * tc_stage_bytes(npad) + 1024; }
+// As many stages as fit the ring budget, at most kTcMaxStages: each CTA
+// streams 512 KB of x per 128 tokens (d = 2048), and the ring depth is what
+// keeps its TMA -> MMA -> release chain from being latency-bound.
+__host__ __device__ constexpr int tc_stages(int npad) {
+  return kTcRingBytes / tc_stage_bytes(npad) < kTcMaxStages ? kTcRingBytes / tc_stage_bytes(npad) : kTcMaxStages;
+}
+__host__ constexpr int tc_smem_bytes(int npad) { return tc_stages(npad) * tc_stage_bytes(npad) + 1024; }
 __host__ __device__ constexpr uint32_t tc_tmem_cols(int npad) {
   return npad <= 32 ? 32u : (npad <= 64 ? 64u : 128u);
 }
@@ -47,13 +54,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) route_tc_kernel(
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int npad = tc_npad(E);
   const int stage_bytes = tc_stage_bytes(npad);
+  const int nstages = tc_stages(npad);
   const uint32_t tmem_cols = tc_tmem_cols(npad);
   // instruction descriptor: f32 accumulate, BF16 A and B, K-major, N = npad, M = 128
   const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(npad >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 
   constexpr int SEL = kMaxTopK * kTcTPB;
-  __shared__ __align__(8) uint64_t full_bar[kTcStages];
-  __shared__ __align__(8) uint64_t empty_bar[kTcStages];
+  __shared__ __align__(8) uint64_t full_bar[kTcMaxStages];
+  __shared__ __align__(8) uint64_t empty_bar[kTcMaxStages];
   __shared__ __align__(8) uint64_t accf_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
@@ -71,7 +79,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) route_tc_kernel(
   const int num_kb = d / 64;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < nstages; ++s) {
       tc::mbar_init(&full_bar[s], 1);
       tc::mbar_init(&empty_bar[s], 1);
     }
@@ -108,7 +116,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) route_tc_kernel(
         tc::mbar_arrive_expect_tx(&full_bar[stage], (uint32_t)stage_bytes);
         tc::tma_load_2d(st, &tmX, &full_bar[stage], kb * 64, tok0);
         tc::tma_load_2d(st + kTcXBytes, &tmG, &full_bar[stage], kb * 64, 0);
-        if (++stage == kTcStages) {
+        if (++stage == nstages) {
           stage = 0;
           phase ^= 1u;
         }
@@ -134,7 +142,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) route_tc_kernel(
           tc::umma_bf16(tmem_base, tc::sdesc_sw128(a0 + kk * 32), tc::sdesc_sw128(b0 + kk * 32), idesc,
                         (kb | kk) != 0 ? 1u : 0u);
         tc::umma_commit(&empty_bar[stage]);
-        if (++stage == kTcStages) {
+        if (++stage == nstages) {
           stage = 0;
           phase ^= 1u;
         }
@@ -216,7 +224,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) route_tc_kernel(
   if (!s_last) return;
   __threadfence();
   // the stage ring is free now: stage the histograms there for the scan
-  const int buf_ints = (kTcStages * stage_bytes) / 4;
+  const int buf_ints = (nstages * stage_bytes) / 4;
   dispatch::scan_segments_block_staged(out.blk_hist, gridDim.x, E, scan.BM, scan.counts, scan.seg_start,
                                        scan.blk_base, scan.mtile_start, s_warp, s_seg, scan.util, k,
                                        reinterpret_cast<int32_t*>(smem), buf_ints);
