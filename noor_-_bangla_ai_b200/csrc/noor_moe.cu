@@ -820,6 +820,12 @@ int ep_exchange(noor_moe_handle* h, cudaStream_t s, int kind, const EpPlan& plan
 // dense GEMM's SMs, so the overlap costs more than the hidden copy time.
 constexpr bool kForkSideSingle = false;
 constexpr bool kForkSidePeer = false;
+// Under the peer-memory exchange, optionally split the permute: the local
+// rows in line, and the rows bound for other ranks (NVLink stores) on a
+// second stream beside the dense up projection.  On two B200s this measured
+// the same as the single in-line permute (24.2-24.4M tokens/s either way),
+// so it is off.
+constexpr bool kSplitPermutePeer = false;
 
 // Wait, bounded, for the setup collectives queued on the handle's stream.
 int setup_sync(noor_moe_handle* h) {
@@ -1064,17 +1070,30 @@ int run_forward_peer(noor_moe_handle* h, cudaStream_t s, const void* x, const CU
     CKR(side_branches());
     CK(cudaEventRecord(h->ev_join, h->aux));
   }
-  if (T > 0) {
-    CKR(launch(h, s, K_PERMUTE, [&] {
+  auto permute = [&](cudaStream_t st, int part, bool persistent) -> int {
+    return launch(h, st, K_PERMUTE, [&] {
       const int64_t blocks = (T + P::kPermuteWarps - 1) / P::kPermuteWarps;
-      const unsigned grid = (unsigned)(fork ? std::min<int64_t>(blocks, h->num_sms) : blocks);
-      P::permute_peer_kernel<<<grid, P::kPermuteWarps * 32, 0, s>>>(
+      const unsigned grid = (unsigned)(persistent ? std::min<int64_t>(blocks, h->num_sms) : blocks);
+      P::permute_peer_kernel<<<grid, P::kPermuteWarps * 32, 0, st>>>(
           static_cast<const uint8_t*>(x), d * 2, (int32_t)T, k, (int32_t)((T + tpb - 1) / tpb), tpb,
           h->idx.as<int32_t>(), h->lrank.as<int32_t>(), h->blk_base.as<int32_t>(), h->seg_start.as<int32_t>(),
-          h->dest_base.as<int32_t>(), h->El, h->peers, h->pstatus.as<int>(), h->dst_row.as<int32_t>());
-    }));
+          h->dest_base.as<int32_t>(), h->El, h->peers, h->pstatus.as<int>(), h->dst_row.as<int32_t>(), part);
+    });
+  };
+  const bool split = kSplitPermutePeer && !fork && T > 0;
+  if (split) {
+    // remote rows on the second stream (persistent grid: it shares the SMs
+    // with the GEMM beside it); local rows and the dense branch in line
+    CK(cudaEventRecord(h->ev_fork, s));
+    CK(cudaStreamWaitEvent(h->aux, h->ev_fork, 0));
+    CKR(permute(h->aux, P::PERMUTE_REMOTE, true));
+    CK(cudaEventRecord(h->ev_join, h->aux));
+    CKR(permute(s, P::PERMUTE_LOCAL, false));
+  } else if (T > 0) {
+    CKR(permute(s, P::PERMUTE_ALL, fork));
   }
   if (side && !fork) CKR(side_branches());  // in line, while the other ranks' rows arrive
+  if (split) CK(cudaStreamWaitEvent(s, h->ev_join, 0));
   auto barrier = [&]() -> int {
     return launch(h, s, K_EP_BARRIER, [&] {
       P::barrier_kernel<<<1, 32, 0, s>>>(h->peers, h->pseq.as<uint64_t>(), h->pstatus.as<int>(), h->d_err);

@@ -279,13 +279,18 @@ __global__ void __launch_bounds__(32) barrier_kernel(Peers P, uint64_t* seq, int
 // expert's output row.  The grid is persistent and small (one 4-warp block
 // per SM, 48 registers a thread) so that it runs beside a tensor-core GEMM
 // that holds the rest of each SM and its NVLink stores overlap that GEMM.
+// part: PERMUTE_ALL, or one of two passes that together do the same work --
+// PERMUTE_LOCAL (rows whose expert lives on this rank, plus every dst_row)
+// and PERMUTE_REMOTE (rows bound for other ranks, over NVLink), which can run
+// on different streams.
 constexpr int kPermuteWarps = 4;
+enum PermutePart : int { PERMUTE_ALL = 0, PERMUTE_LOCAL = 1, PERMUTE_REMOTE = 2 };
 
 __global__ void __launch_bounds__(kPermuteWarps * 32) permute_peer_kernel(
     const uint8_t* __restrict__ x, int32_t row_bytes, int32_t T, int32_t k, int32_t nblk, int32_t tpb,
     const int32_t* __restrict__ idx, const int32_t* __restrict__ lrank, const int32_t* __restrict__ blk_base,
     const int32_t* __restrict__ seg_start, const int32_t* __restrict__ dest_base, int32_t El, Peers P,
-    const int* __restrict__ status, int32_t* __restrict__ dst_row) {
+    const int* __restrict__ status, int32_t* __restrict__ dst_row, int32_t part) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool store = *status == STATUS_OK;
   const int nvec = row_bytes >> 4;
@@ -293,19 +298,24 @@ __global__ void __launch_bounds__(kPermuteWarps * 32) permute_peer_kernel(
   for (int32_t t = blockIdx.x * kPermuteWarps + warp; t < T; t += gridDim.x * kPermuteWarps) {
     uint8_t* dst[8];
     const int32_t* bb = blk_base + t / tpb;  // blk_base[e][block] is bb[e * nblk]
+    bool any = false;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       dst[i] = nullptr;
       if (i < k) {
         const int32_t e = __ldg(idx + (int64_t)t * k + i);
         const int32_t local = __ldg(bb + (int64_t)e * nblk) + __ldg(lrank + (int64_t)t * k + i);
-        if (lane == 0) dst_row[(int64_t)t * k + i] = local;
+        if (lane == 0 && part != PERMUTE_REMOTE) dst_row[(int64_t)t * k + i] = local;
         const int32_t r = e / El;
-        const int32_t remote = __ldg(dest_base + e) + local - __ldg(seg_start + e);
-        dst[i] = P.xrecv[r] + (int64_t)remote * row_bytes;
+        const bool mine = part == PERMUTE_ALL || ((r == P.me) == (part == PERMUTE_LOCAL));
+        if (mine) {
+          const int32_t remote = __ldg(dest_base + e) + local - __ldg(seg_start + e);
+          dst[i] = P.xrecv[r] + (int64_t)remote * row_bytes;
+          any = true;
+        }
       }
     }
-    if (!store) continue;
+    if (!store || !any) continue;
     const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)t * row_bytes);
     for (int base = lane; base < nvec; base += 32 * U) {
       uint4 v[U];
@@ -314,7 +324,7 @@ __global__ void __launch_bounds__(kPermuteWarps * 32) permute_peer_kernel(
         if (base + 32 * u < nvec) v[u] = __ldg(src + base + 32 * u);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        if (i < k) {
+        if (i < k && dst[i] != nullptr) {
           uint4* d = reinterpret_cast<uint4*>(dst[i]);
 #pragma unroll
           for (int u = 0; u < U; ++u)

@@ -35,9 +35,14 @@ def main():
     ap.add_argument("--overflow", action="store_true",
                     help="the last rank first sends a batch above the agreed capacity: every rank must "
                          "report the skipped step, then the next step must be exact")
+    ap.add_argument("--peer-timeout", action="store_true",
+                    help="failure detection: rank 0 runs a forward that the other ranks leave out; its bounded "
+                         "device wait (1 s) must end with NOOR_MOE_ERR_TIMEOUT and close the exchange")
     args = ap.parse_args()
     if args.transport == "nccl":
         os.environ["NOOR_MOE_EP_TRANSPORT"] = "nccl"
+    if args.peer_timeout:
+        os.environ["NOOR_MOE_PEER_TIMEOUT_MS"] = "1000"
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
@@ -65,6 +70,30 @@ def main():
     transport = h.ep_transport
     x = x_of(rank)
     xin = W.bf16_bits(x) if cfg.dtype == W.BF16 else x
+    if args.peer_timeout:
+        outcome, closed = None, None
+        if rank == 0:  # the other ranks never enter the step (no kernel of theirs is in flight)
+            try:
+                h.forward_host(np.ascontiguousarray(xin))
+                outcome = "no error"
+            except pkg.api.NoorMoEError as e:
+                outcome = "timeout" if e.code == 6 else f"code {e.code}"
+            try:
+                h.forward_host(np.ascontiguousarray(xin))
+                closed = False
+            except pkg.api.NoorMoEError as e:
+                closed = e.code == 5  # NOOR_MOE_ERR_STATE: the exchange stays closed
+        dist.barrier()  # rank 0's failed step has ended before any rank frees its buffers
+        h.close()
+        pkg.api.comm_destroy(comm)
+        flags = [None] * world
+        dist.all_gather_object(flags, (transport, outcome, closed))
+        ok = flags[0][0] == "peer" and flags[0][1] == "timeout" and flags[0][2] is True
+        if rank == 0:
+            print(json.dumps({"world": world, "peer_timeout": [f[1:] for f in flags], "ok": ok}), flush=True)
+        dist.barrier()
+        dist.destroy_process_group()
+        return 0 if ok else 1
     overflow = None
     if args.overflow:
         # capacity = the largest max_tokens over the ranks, rounded up to 128

@@ -28,6 +28,7 @@ def _run(n, *extra):
     ("--transport", "peer", "--graph"),             # BF16: NVLink peer-memory exchange, eager + CUDA graph
     ("--transport", "peer", "--uneven"),            # one rank with no tokens, the others ragged
     ("--transport", "peer", "--overflow"),          # an over-capacity batch is refused on every rank, then exact
+    ("--transport", "peer", "--peer-timeout"),      # a rank that never joins: bounded wait, TIMEOUT, exchange closed
     ("--transport", "nccl"),                        # the NCCL all-to-all-v exchange
     ("--transport", "nccl", "--uneven"),
     ("--config", "proxy_tiny", "--tokens", "777"),  # F32 layer (NCCL exchange)
