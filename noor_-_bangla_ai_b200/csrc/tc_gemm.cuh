@@ -355,11 +355,45 @@ __device__ __forceinline__ void combine_chunk32(const Params& p, int row, int co
 // With `stage` (4 KB of shared memory for this warp) BF16 outputs leave
 // through write_chunk32_staged (write_chunk64_staged for the plain store);
 // without it each thread stores its own row.
+// The fused combine's per-token inputs for one epilogue warp's rows of a
+// tile: each pick's row of y and weight, and an L2 prefetch of the warp's
+// column range of those rows.  The epilogue calls it before it waits for the
+// tile's accumulator, so the gathers of y overlap the tile's MMAs and the
+// chunk loop finds them in L2.
+template <int BN>
+__device__ __forceinline__ void combine_prepare(const Params& p, int32_t row0, int32_t rows, int32_t nt, int q,
+                                                int part, int lane, int32_t (&dst)[8], float (&wv)[8]) {
+  constexpr int SPAN = BN / 2;
+  const int row_in_tile = q * 32 + lane;
+  const bool valid = row_in_tile < rows;
+  const int row = row0 + row_in_tile;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    dst[i] = 0;
+    wv[i] = 0.f;
+    if (valid && i < p.k) {
+      dst[i] = __ldg(p.dst_row + (int64_t)row * p.k + i);
+      wv[i] = __ldg(p.wts + (int64_t)row * p.k + i);
+    }
+  }
+  if (valid) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i < p.k) {
+        const char* yrow = reinterpret_cast<const char*>(p.y + (int64_t)dst[i] * p.ldc + nt * BN + part * SPAN);
+#pragma unroll
+        for (int off = 0; off < SPAN * 2; off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(yrow + off));
+      }
+    }
+  }
+}
+
 // Outputs go to rows + shift of C (the combine reads its inputs at the
-// unshifted rows).
+// unshifted rows).  cdst / cwv: the combine's inputs from combine_prepare.
 template <int BN, int EPI>
 __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t shift, uint32_t t_base, int32_t row0,
-                                              int32_t rows, int32_t nt, int q, int part, int lane, uint8_t* stage) {
+                                              int32_t rows, int32_t nt, int q, int part, int lane, uint8_t* stage,
+                                              const int32_t (&cdst)[8], const float (&cwv)[8]) {
   const int row_in_tile = q * 32 + lane;
   const bool valid = row_in_tile < rows;
   const int row = row0 + row_in_tile;
@@ -382,37 +416,13 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
     }
   } else if constexpr (EPI == EPI_COMBINE_BF16) {
     constexpr int SPAN = BN / 2;
-    int32_t dst[8];
-    float wv[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      dst[i] = 0;
-      wv[i] = 0.f;
-      if (valid && i < p.k) {
-        dst[i] = __ldg(p.dst_row + (int64_t)row * p.k + i);
-        wv[i] = __ldg(p.wts + (int64_t)row * p.k + i);
-      }
-    }
-    // Bring this warp's whole column range of the k gathered rows into L2
-    // before the chunk loop, so that each chunk's loads wait on L2, not DRAM.
-    if (valid) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (i < p.k) {
-          const char* yrow = reinterpret_cast<const char*>(p.y + (int64_t)dst[i] * p.ldc + nt * BN + part * SPAN);
-#pragma unroll
-          for (int off = 0; off < SPAN * 2; off += 128)
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(yrow + off));
-        }
-      }
-    }
 #pragma unroll 1
     for (int c = part * SPAN; c < (part + 1) * SPAN; c += 32) {
       uint32_t g[32];
       tmem_ld32(t_base + c, g);
       tmem_ld_wait();
       uint32_t pk[16];
-      combine_chunk32(p, row, nt * BN + c, valid, g, dst, wv, pk);
+      combine_chunk32(p, row, nt * BN + c, valid, g, cdst, cwv, pk);
       if (stage) write_chunk32_staged(C, p.ldc, wrow0, wrows, nt * BN + c, pk, stage, lane);
       else if (valid) write_chunk32_direct(C, p.ldc, orow, nt * BN + c, pk);
     }
@@ -592,13 +602,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t acc_phase = 0;
     for (int32_t tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
       const TileCoord tc = decode_tile(groups, tile, p.n_tiles, BM);
+      int32_t cdst[8];
+      float cwv[8];
+      if constexpr (EPI == EPI_COMBINE_BF16) combine_prepare<BN>(p, tc.row0, tc.rows, tc.nt, q, part, lane, cdst, cwv);
       if (!mbar_wait(&accf_bar[acc], acc_phase, &abort_flag, p.err, DEV_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t t_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       void* Ct;
       int32_t shift;
       tile_output(p, tc.g, &Ct, &shift);
-      epilogue_tile<BN, EPI>(p, Ct, shift, t_base, tc.row0, tc.rows, tc.nt, q, part, lane, nullptr);
+      epilogue_tile<BN, EPI>(p, Ct, shift, t_base, tc.row0, tc.rows, tc.nt, q, part, lane, nullptr, cdst, cwv);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce_bar[acc]);
@@ -852,14 +865,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     uint32_t acc_phase = 0;
     for (int32_t tile = cid; tile < total_tiles; tile += nclusters) {
       const TileCoord tc = decode_tile(groups, tile, p.n_tiles, BM2);
+      const int32_t row0 = tc.row0 + 128 * (int32_t)rank, rows = tc.rows - 128 * (int32_t)rank;
+      int32_t cdst[8];
+      float cwv[8];
+      if constexpr (EPI == EPI_COMBINE_BF16) combine_prepare<BN>(p, row0, rows, tc.nt, q, part, lane, cdst, cwv);
       if (!mbar_wait(&accf_bar[acc], acc_phase, &abort_flag, p.err, DEV_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t t_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       void* Ct;
       int32_t shift;
       tile_output(p, tc.g, &Ct, &shift);
-      epilogue_tile<BN, EPI>(p, Ct, shift, t_base, tc.row0 + 128 * (int32_t)rank, tc.rows - 128 * (int32_t)rank,
-                             tc.nt, q, part, lane, smOut + (warp - 2) * C::STAGE_OUT_BYTES);
+      epilogue_tile<BN, EPI>(p, Ct, shift, t_base, row0, rows, tc.nt, q, part, lane,
+                             smOut + (warp - 2) * C::STAGE_OUT_BYTES, cdst, cwv);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
