@@ -1012,12 +1012,14 @@ int peer_setup(noor_moe_handle* h) {
 }
 
 // The layer step under expert parallelism over peer memory (BF16), without
-// host synchronization:
+// host synchronization, on one stream:
 //   router -> plan (counts to every rank, barrier, tables) -> permute (rows
-//   into the owners' receive buffers; beside it, on a second stream, the
-//   dense/shared up projections) -> barrier -> expert GEMM 1 -> expert
+//   into the owners' receive buffers) -> dense/shared up projections (while
+//   the other ranks' rows arrive) -> barrier -> expert GEMM 1 -> expert
 //   GEMM 2 (outputs back to the senders) -> barrier -> dense down
 //   projection with the fused combine.
+// kForkSidePeer / kSplitPermutePeer move the side branches or the remote
+// rows to a second stream instead (both measured no faster).
 // Every rank runs the plan and both barriers, with or without tokens.
 int run_forward_peer(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtensorMap* tmx, void* out,
                      int64_t T) {
@@ -1046,9 +1048,7 @@ int run_forward_peer(noor_moe_handle* h, cudaStream_t s, const void* x, const CU
                 "max_tokens given at creation); every rank skipped this step",
                 (long long)T, (long long)h->capP);
   }
-  // The side branches (dense up projection, shared expert) need only x: they
-  // run on a second stream beside the permute, whose NVLink stores then
-  // overlap a tensor-core GEMM.
+  // The side branches (dense up projection, shared expert) need only x.
   const GluFfn dense{K_DENSE_GEMM1, K_DENSE_GEMM2, tmx, x, T, h->dff, h->desc.dense_act == NOOR_ACT_SILU,
                      &h->tm_dw1, &h->tm_dw2, &h->tm_dh, nullptr, nullptr, nullptr, h->dense_h.p};
   const GluFfn shared{K_SHARED_GEMM1, K_SHARED_GEMM2, tmx, x, T, h->ff, true, &h->tm_sw1, &h->tm_sw2, &h->tm_sh,
@@ -1132,9 +1132,10 @@ int run_forward_peer(noor_moe_handle* h, cudaStream_t s, const void* x, const CU
 
 // x, out: device pointers of the layer dtype.  tmx: tensor map of x (BF16).
 //
-// One GPU: a single stream, in dependency order.  Expert parallel: the dense
-// (and shared) up projections run on a second stream while the rows cross
-// NVLink; the dense down projection waits for the returned expert rows.
+// One GPU: a single stream, in dependency order.  Expert parallel over peer
+// memory: run_forward_peer.  Expert parallel over NCCL: the dense (and
+// shared) up projections run on a second stream while the rows cross; the
+// dense down projection waits for the returned expert rows.
 int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtensorMap* tmx, void* out, int64_t T) {
   if (h->peer) return run_forward_peer(h, s, x, tmx, out, T);
   const int d = h->d, k = h->k, E = h->E;
