@@ -10,6 +10,15 @@ experts are sharded expert-parallel E/N per rank and every rank routes its own
 batch: the Edge-like layer keeps 16384 tokens per rank (weak scaling), the
 Pro-like layer splits its 131072 tokens across ranks (strong scaling).
 
+`value` is device-resident throughput: the timed steps replay one captured
+forward (a CUDA graph; plain calls under the NCCL exchange), with L2 flushed
+between steps and the time taken with CUDA events, the max over ranks.  `e2e`
+is the same forward through the public API with each step's input uploaded
+from pinned host memory and its output downloaded, inside the timed region:
+pipelined over two buffers (the reported value) and serialised
+(`serial_value`).  `kernels` and `roofline` come from the library's own
+per-launch events on an uncaptured pass.
+
 `--impl reference` times the reference's CPU algorithm for the same layer (the
 oracle port of crates/noor-core MoELayer/ParallelFFN, per-token m=1 OpenBLAS
 sgemm as the reference's cblas route) on this host's cores, on rank 0 only.

@@ -281,6 +281,7 @@ NOOR_MOE_API int64_t noor_moe_launch_count(const noor_moe_handle* h);
  *   x       [T, d]  f32 (dtype F32) or BF16 bits (dtype BF16)
  *   gate    F32: [d, E] f32, the reference layout (moe.rs:7);
  *           BF16: [roundup(E, 8), d] BF16 bits, the gate transposed, rows >= E zero
+ *   (BF16: x and gate 16-byte aligned; the tensor cores read them through TMA)
  *   bias, scales [E] f32;  outputs idx [T, k] int32, w [T, k] f32, counts [E] int64.
  * Working memory comes from one fixed array of NOOR_MOE_STATIC_SCRATCH_BYTES
  * per GPU; a call whose T, E, k would need more returns NOOR_MOE_ERR_INVALID
