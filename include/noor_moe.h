@@ -106,7 +106,9 @@ NOOR_MOE_API int noor_moe_set_bias(noor_moe_handle* h, const float* bias);
  *   topk_w   [T, k] f32     RouteResult::weights = sigmoid score * scale
  *   expert_counts [E] int64 this call's ExpertUtilization::record counts
  *                           (moe.rs:40-45), summed over all ranks under EP
- * In device mode (stream != NULL) all pointers are device pointers.
+ * In device mode (stream != NULL) all pointers are device pointers; for BF16
+ * layers x and out must be 16-byte aligned (the tensor cores read x through
+ * TMA), else NOOR_MOE_ERR_INVALID.
  * Under expert parallelism every rank calls this collectively with its own
  * T tokens. */
 NOOR_MOE_API int noor_moe_forward(noor_moe_handle* h, const void* x, void* out, int64_t T, int32_t* topk_idx,
