@@ -7,6 +7,7 @@ The compute lives in libnoor_moe.so (csrc/, C ABI in include/noor_moe.h);
 from . import workloads  # noqa: F401
 from . import api  # noqa: F401
 from . import gguf  # noqa: F401
+from . import stack  # noqa: F401
 from .api import (ExpertUtilization, GeGLUFFN, Handle, MoELayer, MoERouter, NoorMoEError,  # noqa: F401
                   ParallelFFN, RMSNorm, RouteResult, SandwichNorm, SMEBU, SwiGLUFFN, ffn_sublayer_forward,
                   matmul_f32)

@@ -292,3 +292,137 @@ def np_parallel_forward(w, x, top_k: int):
     ge = 0.5 * gg * (1.0 + np.tanh(c * (gg + 0.044715 * gg ** 3)))
     dense = (ge * uu) @ w.dense_down.astype(np.float64)
     return (dense + moe) / np.sqrt(2.0), order.astype(np.int32), wt
+
+
+# ------------------------------------------------- the decoder stack around the layer
+# RoPE::apply (rope.rs:49-90), GQAAttention::forward without a KV cache
+# (attention.rs:67-191), MoEBlock::forward (block.rs:74-97) and the model
+# forward (model.rs:127-207), restated in f32 with the reference's operation
+# order.  Rust's f32 cos / sin / exp call libm's cosf / sinf / expf, which
+# these use too.  Loops are plain Python: small configurations only.
+
+_libm = None
+
+
+def _m():
+    global _libm
+    if _libm is None:
+        _libm = ctypes.CDLL("libm.so.6")
+        for f in ("cosf", "sinf", "expf"):
+            getattr(_libm, f).argtypes = [ctypes.c_float]
+            getattr(_libm, f).restype = ctypes.c_float
+    return _libm
+
+
+def rope_inv_freq(head_dim: int, theta: float, fraction: Optional[float] = None):
+    """RoPE::new / new_proportional (rope.rs:17-45)."""
+    rotate_dim = head_dim if fraction is None else max(2, (int(head_dim * fraction) // 2) * 2)
+    inv = np.array([np.float32(1.0) / np.float32(theta ** (2.0 * i / rotate_dim))
+                    for i in range(rotate_dim // 2)], np.float32)
+    return inv, rotate_dim
+
+
+def rope_apply(x, inv_freq, rotate_dim: int, seq_offset: int = 0) -> np.ndarray:
+    """RoPE::apply (rope.rs:49-90) on x (..., seq, head_dim), f32."""
+    x = _f32(x)
+    out = x.copy()
+    m = _m()
+    for s in range(x.shape[-2]):
+        pos = np.float32(seq_offset + s)
+        for i in range(rotate_dim // 2):
+            ang = np.float32(pos * inv_freq[i])
+            c, sn = np.float32(m.cosf(float(ang))), np.float32(m.sinf(float(ang)))
+            x0, x1 = x[..., s, 2 * i], x[..., s, 2 * i + 1]
+            out[..., s, 2 * i] = (x0 * c).astype(np.float32) - (x1 * sn).astype(np.float32)
+            out[..., s, 2 * i + 1] = (x0 * sn).astype(np.float32) + (x1 * c).astype(np.float32)
+    return out
+
+
+def gqa_attention(x, wq, wk, wv, wo, n_heads: int, n_kv_heads: int, head_dim: int, sliding_window: int,
+                  inv_freq, rotate_dim: int):
+    """GQAAttention::forward (attention.rs:67-191), one sequence, no cache.
+    Returns (output [seq, d], max_attn_logit)."""
+    x = _f32(x)
+    S = x.shape[0]
+    nh, nkv, hd = n_heads, n_kv_heads, head_dim
+    q = matmul(x, wq).reshape(S, nh, hd).transpose(1, 0, 2).copy()
+    k = matmul(x, wk).reshape(S, nkv, hd).transpose(1, 0, 2).copy()
+    v = matmul(x, wv).reshape(S, nkv, hd).transpose(1, 0, 2).copy()
+    q = rope_apply(q, inv_freq, rotate_dim)
+    k = rope_apply(k, inv_freq, rotate_dim)
+    scale = np.float32(1.0) / np.sqrt(np.float32(hd))
+    out = np.zeros((nh, S, hd), np.float32)
+    max_logit = np.float32(-np.inf)
+    m = _m()
+    group = nh // nkv
+    for qh in range(nh):
+        kv = qh // group
+        for sq in range(S):
+            scores = np.full(S, -np.inf, np.float32)
+            for sk in range(S):
+                if sk > sq or (sliding_window > 0 and sq > sk + sliding_window):
+                    continue
+                dot = np.float32(0.0)
+                for dd in range(hd):
+                    dot = np.float32(dot + np.float32(q[qh, sq, dd] * k[kv, sk, dd]))
+                scores[sk] = np.float32(dot * scale)
+                max_logit = max(max_logit, scores[sk])
+            max_s = scores.max()
+            p = np.array([0.0 if s_ == -np.inf else m.expf(float(np.float32(s_ - max_s))) for s_ in scores],
+                         np.float32)
+            tot = np.float32(0.0)
+            for p_ in p:
+                tot = np.float32(tot + p_)
+            if tot > 0:
+                p = (p / tot).astype(np.float32)
+            for dd in range(hd):
+                val = np.float32(0.0)
+                for sk in range(S):
+                    if p[sk] > 0:
+                        val = np.float32(val + np.float32(p[sk] * v[kv, sk, dd]))
+                out[qh, sq, dd] = val
+    attn = out.transpose(1, 0, 2).reshape(S, nh * hd).copy()
+    return matmul(attn, wo), float(max_logit)
+
+
+def _bf16_storage(a):
+    u = _f32(a).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16  # RNE (tensor.rs:23-28), finite values
+    return (u.astype(np.uint32) << np.uint32(16)).view(np.float32)
+
+
+def moe_block_forward(blk, x, eps: float, inv_freq, rotate_dim: int, bf16_storage: bool):
+    """MoEBlock::forward (block.rs:74-97).  blk: dict with the attention
+    weights / head counts / window, the four norm weights, depth_scale, the
+    layer's LayerWeights `w` and top_k.  With bf16_storage the residual
+    stream is rounded to BF16 after each sublayer, as a BF16 layer stores
+    it."""
+    ds = np.float32(blk["depth_scale"])
+    normed = (rms_norm(x, blk["attn_pre"], eps) * ds).astype(np.float32)
+    a, ml = gqa_attention(normed, blk["wq"], blk["wk"], blk["wv"], blk["wo"], blk["n_heads"], blk["n_kv_heads"],
+                          blk["head_dim"], blk["window"], inv_freq, rotate_dim)
+    a = (rms_norm(a, blk["attn_post"], eps) * ds).astype(np.float32)
+    h = (_f32(x) + a).astype(np.float32)
+    if bf16_storage:
+        h = _bf16_storage(h)
+    out, _idx, _wt, counts, _xn = ffn_sublayer_forward(blk["w"], h, blk["top_k"], blk["ffn_pre"], blk["ffn_post"],
+                                                        eps, float(ds), bf16_storage)
+    if bf16_storage:
+        out = _bf16_storage(out)
+    return out, ml, counts
+
+
+def stack_forward(embedding, blocks, final_norm, output_proj, token_ids, eps: float, ropes, bf16_storage: bool):
+    """The model forward (model.rs:127-207) over MoE blocks: embedding lookup
+    (embedding.rs:19-35), the blocks (ropes[i] = (inv_freq, rotate_dim) of
+    layer i), the final RMSNorm and the output projection.  Returns (logits,
+    max_attn_logit)."""
+    h = _f32(embedding)[np.asarray(token_ids)]
+    if bf16_storage:
+        h = _bf16_storage(h)
+    ml = -np.inf
+    for blk, (inv, rd) in zip(blocks, ropes):
+        h, m_, _ = moe_block_forward(blk, h, eps, inv, rd, bf16_storage)
+        ml = max(ml, m_)
+    h = rms_norm(h, final_norm, eps)
+    return matmul(h, output_proj), ml
