@@ -90,9 +90,16 @@ static int fail(int code, const char* fmt, ...) {
 
 // ============================================================== device buffers
 
+// A device allocation owned by one object: freed by release() or, at the
+// latest, when the object goes out of scope (function-local staging buffers,
+// the handle's buffers after destroy() released them).  Not copyable.
 struct DevBuf {
   void* p = nullptr;
   size_t bytes = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  ~DevBuf() { release(); }
   int ensure(size_t n) {
     if (n <= bytes) return NOOR_MOE_OK;
     if (p) cudaFree(p);
