@@ -18,6 +18,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <nccl.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <chrono>
@@ -329,13 +330,16 @@ struct DeviceGuard {
   }
 };
 
-// Launch wrapper: brackets the launch with profile events when enabled and
-// counts it.
+// Launch wrapper: names the launch with an NVTX range (seen by ncu / nsys;
+// a no-op without a tool attached), brackets it with profile events when
+// enabled and counts it.
 template <typename F>
 int launch(noor_moe_handle* h, cudaStream_t s, int kind, F&& f) {
   const bool prof = h->prof_on && h->prof_used < h->prof_cap;
   if (prof) CK(cudaEventRecord(h->prof_ev[2 * h->prof_used], s));
+  nvtxRangePushA(kKindNames[kind]);
   f();
+  nvtxRangePop();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(NOOR_MOE_ERR_CUDA, "launch of %s failed: %s", kKindNames[kind], cudaGetErrorString(e));
   if (prof) {
@@ -352,7 +356,10 @@ template <typename F>
 int timed_phase(noor_moe_handle* h, cudaStream_t s, int kind, F&& f) {
   const bool prof = h->prof_on && h->prof_used < h->prof_cap;
   if (prof) CK(cudaEventRecord(h->prof_ev[2 * h->prof_used], s));
-  CKR(f());
+  nvtxRangePushA(kKindNames[kind]);
+  const int rc = f();
+  nvtxRangePop();
+  CKR(rc);
   if (prof) {
     CK(cudaEventRecord(h->prof_ev[2 * h->prof_used + 1], s));
     h->prof_kind[h->prof_used] = kind;
