@@ -60,3 +60,22 @@ def test_stack_matches_oracle(pkg, oracle, dtype_name, tol):
         assert abs(sum(f) - 2.0) < 1e-5
     for b in st.blocks:
         b.parallel_ffn.moe.invalidate()
+
+
+def test_reference_block_tests(pkg):
+    """block.rs:198-212 and 273-281 through the mirror: a small F32 MoE block
+    (shared expert on) keeps the shape, and its max attention logit is finite."""
+    api = pkg.api
+    rng = np.random.default_rng(11)
+    blk = pkg.stack.MoEBlock(32, 4, 2, 8, 64, 32, 4, 2, True, 16, 0, False, 1e-6, 0.02, dtype=api.DTYPE_F32,
+                             rng=rng)
+    rope = pkg.stack.RoPE(8, 10000.0)
+    x = torch.randn(4, 32, device="cuda")
+    out, ml = blk.forward(x, rope)
+    assert tuple(out.shape) == (4, 32) and torch.isfinite(out).all()
+    blk2 = pkg.stack.MoEBlock(16, 2, 1, 8, 32, 16, 4, 2, False, 0, 0, False, 1e-6, 0.5, dtype=api.DTYPE_F32,
+                              rng=rng)
+    out2, ml2 = blk2.forward(torch.randn(3, 16, device="cuda"), rope)
+    assert np.isfinite(ml2) and tuple(out2.shape) == (3, 16)
+    for b in (blk, blk2):
+        b.parallel_ffn.moe.invalidate()
