@@ -1,14 +1,16 @@
 """MoE-layer forward throughput on B200 (tokens/s), one JSON line on rank 0.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--config edge|edge_skewed|pro|proxy_tiny]
-                  [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W]
+                  [--config edge|edge_skewed|pro|max_layer|proxy_tiny] [--impl ours|reference]
+                  [--no-pro] [--no-cpu-baseline] [--no-graph]
 
 A step is one ParallelFFN forward (router, permute, grouped SwiGLU expert
 GEMMs, dense GeGLU branch, combine) over one batch of seeded synthetic tokens,
 all inputs resident in HBM.  With N > 1 (torchrun, one process per GPU) the
 experts are sharded expert-parallel E/N per rank and every rank routes its own
-batch: the Edge-like layer keeps 16384 tokens per rank (weak scaling), the
-Pro-like layer splits its 131072 tokens across ranks (strong scaling).
+batch: the Edge-like and Max-like layers keep their tokens per rank (weak
+scaling), the Pro-like layer splits its 131072 tokens across ranks (strong
+scaling).
 
 `value` is device-resident throughput: the timed steps replay one captured
 forward (a CUDA graph; plain calls under the NCCL exchange), with L2 flushed
@@ -17,7 +19,15 @@ is the same forward through the public API with each step's input uploaded
 from pinned host memory and its output downloaded, inside the timed region:
 pipelined over two buffers (the reported value) and serialised
 (`serial_value`).  `kernels` and `roofline` come from the library's own
-per-launch events on an uncaptured pass.
+per-launch events on an uncaptured pass; tensor-core fractions divide by the
+burst cuBLAS peak (the kernels run inside a ~1 ms step at full clock), with a
+per-GHz figure beside them.
+
+After the headline layer the same run times the Pro-like layer (BASELINE
+config 4, strong scaling over the N GPUs) into the `pro` key, unless
+--no-pro or the headline is Pro-like itself.  Under expert parallelism every
+rank then checks its output bit for bit against a single-GPU handle holding
+all experts (`ep_parity`).
 
 `--impl reference` times the reference's CPU algorithm for the same layer (the
 oracle port of crates/noor-core MoELayer/ParallelFFN, per-token m=1 OpenBLAS
@@ -26,9 +36,9 @@ sgemm as the reference's cblas route) on this host's cores, on rank 0 only.
 from __future__ import annotations
 
 import argparse
+import datetime
 import importlib
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -47,6 +57,7 @@ UNIT = "tokens/s"
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_FLUSH_BYTES = 256 << 20
+PRO_STEPS = 10  # timed steps of the extra Pro-like pass
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one expert
 # GEMM 1 launch, from an ncu --set full capture of this kernel on the
@@ -74,6 +85,16 @@ def layer_tokens(cfg, world):
     if cfg.name == "pro":
         return cfg.tokens // world, "strong"
     return cfg.tokens, "weak"
+
+
+def config_dict(cfg, T_rank, world, scaling):
+    """The workload; identical in both arms for the same --config and N."""
+    return {"workload": f"{cfg.name} MoE layer (ParallelFFN forward)", "tokens_per_rank": T_rank,
+            "global_tokens": T_rank * world, "d_model": cfg.d_model, "n_experts": cfg.n_experts,
+            "top_k": cfg.top_k, "expert_ff": cfg.expert_ff, "dense_ff": cfg.dense_ff,
+            "dense_act": "gelu_tanh (GeGLU)", "parallelism": f"ep{world}" if world > 1 else "single",
+            "experts_per_rank": cfg.n_experts // world, "l2": "flushed (256 MiB write between steps, "
+            "outside the timed events)", "scaling": scaling}
 
 
 # ------------------------------------------------------------------ clocks
@@ -124,25 +145,33 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ CPU baseline
 
-def cpu_baseline(cfg, w, x_sample, steps: int = 1):
-    """The oracle port of the reference path on this host's cores, OpenBLAS
-    threads = all cores; returns (tokens/s, cores, seconds)."""
+CPU_MOE_SAMPLE = {"proxy_tiny": 2048, "edge": 2048, "edge_skewed": 2048, "pro": 256, "max_layer": 128}
+
+
+def cpu_baseline(cfg, w, x):
+    """The reference's path on this host's cores (oracle port, OpenBLAS with
+    all cores): the dense GeGLU branch over all T tokens, as the reference
+    runs it (three batched sgemm, ffn.rs:24-34), plus the per-token MoE loop
+    (moe.rs:145-177, m=1 sgemm per expert) over a contiguous sample of the
+    batch, extrapolated linearly to T (the loop carries no state across
+    tokens).  Returns (tokens/s, cores, seconds spent, sample tokens, blas)."""
     from oracle import oracle as O
     cores = os.cpu_count() or 1
+    T = x.shape[0]
+    n = min(T, CPU_MOE_SAMPLE.get(cfg.name, 512))
     blas = O.use_openblas(cores)
     try:
-        O.parallel_forward(w, x_sample[:8], cfg.top_k)  # warm the BLAS
+        O.moe_forward(w, x[:4], cfg.top_k)  # warm the BLAS
         t0 = time.perf_counter()
-        for _ in range(steps):
-            O.parallel_forward(w, x_sample, cfg.top_k)
-        dt = time.perf_counter() - t0
+        O.glu_ffn(x, w.dense_gate, w.dense_up, w.dense_down, 0)
+        t_dense = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        O.moe_forward(w, np.ascontiguousarray(x[:n]), cfg.top_k)
+        t_moe = time.perf_counter() - t0
     finally:
         O.use_plain_loops()
-    return x_sample.shape[0] * steps / dt, (cores if blas else 1), dt, blas
-
-
-def cpu_sample_tokens(cfg):
-    return {"proxy_tiny": 2048, "edge": 512, "edge_skewed": 512, "pro": 256}.get(cfg.name, 512)
+    total = t_dense + t_moe * T / n
+    return T / total, (cores if blas else 1), t_dense + t_moe, n, blas
 
 
 # ------------------------------------------------------------------ reference arm
@@ -169,7 +198,7 @@ def run_reference(args):
         O.parallel_forward(w, cal, cfg.top_k)
         tps = 64 / max(time.perf_counter() - t0, 1e-6)
         n = int(REFERENCE_BUDGET_S * tps / max(1, args.steps + args.warmup))
-        n = max(16, min(cpu_sample_tokens(cfg), n))
+        n = max(16, min(CPU_MOE_SAMPLE.get(cfg.name, 512), n))
         x = W.make_tokens(cfg, tokens=n)
         for i in range(args.warmup + args.steps):
             t0 = time.perf_counter()
@@ -198,45 +227,67 @@ def run_reference(args):
     return 0
 
 
-def config_dict(cfg, T_rank, world, scaling):
-    return {"workload": f"{cfg.name} MoE layer (ParallelFFN forward)", "tokens_per_rank": T_rank,
-            "global_tokens": T_rank * world, "d_model": cfg.d_model, "n_experts": cfg.n_experts,
-            "top_k": cfg.top_k, "expert_ff": cfg.expert_ff, "dense_ff": cfg.dense_ff,
-            "dense_act": "gelu_tanh (GeGLU)", "parallelism": f"ep{world}" if world > 1 else "single",
-            "experts_per_rank": cfg.n_experts // world, "l2": "flushed (256 MiB write between steps, "
-            "outside the timed events)", "scaling": scaling}
-
-
 # ------------------------------------------------------------------ our arm
 
-def run_ours(args):
-    import torch
-    import torch.distributed as dist
+class Ctx:
+    """Per-process state shared by the layers this run measures."""
 
-    rank, local_rank, world = env_rank()
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=300))
-    cfg = W.CONFIGS[args.config]
+    def __init__(self, torch, dist, rank, local_rank, world, dev):
+        self.torch, self.dist = torch, dist
+        self.rank, self.local_rank, self.world, self.dev = rank, local_rank, world, dev
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+        self.torch.cuda.synchronize(self.dev)
+
+    def max_over_ranks(self, *vals):
+        if self.world == 1:
+            return list(vals)
+        t = self.torch.tensor(list(vals), dtype=self.torch.float64, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return [float(v) for v in t.cpu().tolist()]
+
+    def sum_over_ranks(self, v: int) -> int:
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.int64, device=self.dev)
+        self.dist.all_reduce(t)
+        return int(t.item())
+
+    def all_ranks_true(self, ok: bool) -> bool:
+        if self.world == 1:
+            return ok
+        t = self.torch.tensor([1 if ok else 0], dtype=self.torch.int64, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MIN)
+        return bool(t.item())
+
+    def new_comm(self):
+        if self.world == 1:
+            return None
+        torch = self.torch
+        uid = pkg.api.comm_get_id() if self.rank == 0 else bytes(pkg.api.lib().noor_moe_comm_id_size())
+        t = torch.tensor(list(uid), dtype=torch.uint8, device=self.dev)
+        self.dist.broadcast(t, 0)
+        return pkg.api.comm_init_rank(bytes(t.cpu().tolist()), self.world, self.rank, self.local_rank)
+
+
+def measure_layer(ctx, cfg, steps, warmup, use_graph, want_e2e, want_parity, clocks=None):
+    """Times one layer's forward over `steps` steps on every rank; returns the
+    numbers for rank 0's line (value, ms/step, launches, per-kernel times, e2e,
+    ep_parity)."""
+    torch = ctx.torch
+    dev, world, rank = ctx.dev, ctx.world, ctx.rank
     T, scaling = layer_tokens(cfg, world)
     w = W.make_weights(cfg)
     x = W.make_tokens(cfg, seed_offset=1 + 7919 * rank, tokens=T)
     xb = W.bf16_bits(x) if cfg.dtype == W.BF16 else x
-
-    comm = None
-    if world > 1:
-        uid = pkg.api.comm_get_id() if rank == 0 else bytes(pkg.api.lib().noor_moe_comm_id_size())
-        t = torch.tensor(list(uid), dtype=torch.uint8, device=dev)
-        dist.broadcast(t, 0)
-        comm = pkg.api.comm_init_rank(bytes(t.cpu().tolist()), world, rank, local_rank)
+    comm = ctx.new_comm()
     h = pkg.api.Handle(cfg.d_model, cfg.n_experts, cfg.top_k, cfg.expert_ff, cfg.dense_ff, dtype=cfg.dtype,
-                       device=local_rank, world_size=world, rank=rank, max_tokens=T, comm=comm)
+                       device=ctx.local_rank, world_size=world, rank=rank, max_tokens=T, comm=comm)
     h.load_weights(w)
 
-    tdt = torch.int16 if cfg.dtype == W.BF16 else torch.float32
     x_host = torch.from_numpy(xb.view(np.int16) if cfg.dtype == W.BF16 else xb).pin_memory()
-    out_host = torch.empty_like(x_host).pin_memory()
     x_dev = x_host.to(dev)
     out_dev = torch.empty_like(x_dev)
     counts = torch.empty(cfg.n_experts, dtype=torch.int64, device=dev)
@@ -247,15 +298,10 @@ def run_ours(args):
     def step():
         h.forward_device(x_dev.data_ptr(), out_dev.data_ptr(), T, sid, counts_ptr=counts.data_ptr())
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         flush.zero_()
         step()
-    barrier()
+    ctx.barrier()
 
     # The timed steps replay one captured forward (a CUDA graph) on one GPU
     # and under expert parallelism over peer memory; the NCCL exchange waits
@@ -263,7 +309,7 @@ def run_ours(args):
     transport = h.ep_transport
     graph = None
     launches_per_step = None
-    if transport in ("none", "peer") and not args.no_graph:
+    if transport in ("none", "peer") and use_graph:
         cs = torch.cuda.Stream(dev)
         cs.wait_stream(stream)
         with torch.cuda.stream(cs):
@@ -274,22 +320,22 @@ def run_ours(args):
         with torch.cuda.graph(graph, stream=cs):
             h.forward_device(x_dev.data_ptr(), out_dev.data_ptr(), T, cs.cuda_stream, counts_ptr=counts.data_ptr())
         launches_per_step = h.launch_count() - l0
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             flush.zero_()
             graph.replay()
-        barrier()
+        ctx.barrier()
 
     # ---- timed region: device events around each step, L2 flushed in between
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    sampler = ClockSampler(local_rank)
-    sampler.start()
-    time.sleep(0.3)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    if clocks is not None:
+        clocks.start()
+        time.sleep(0.3)
     launches0 = h.launch_count()
     if graph is None:
-        h.profile_begin(args.steps * 16)
-    barrier()
-    for i in range(args.steps):
+        h.profile_begin(steps * 16)
+    ctx.barrier()
+    for i in range(steps):
         flush.zero_()
         starts[i].record(stream)
         if graph is None:
@@ -297,32 +343,44 @@ def run_ours(args):
         else:
             graph.replay()
         ends[i].record(stream)
-    barrier()
-    clocks = sampler.stop()
+    ctx.barrier()
+    clock_rec = clocks.stop() if clocks is not None else None
     if graph is None:
         prof = h.profile_end()
         launches = h.launch_count() - launches0
     else:
-        launches = launches_per_step * args.steps
+        launches = launches_per_step * steps
         # per-kernel times: the same forward, uncaptured, with an event pair
         # around each of its kernels
-        prof_steps = min(args.steps, 200)
+        prof_steps = min(steps, 200)
         h.profile_begin(prof_steps * 16)
         for i in range(prof_steps):
             flush.zero_()
             step()
-        barrier()
+        ctx.barrier()
         prof = h.profile_end()
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    tot_ms = sum(step_ms)
-    if world > 1:
-        tt = torch.tensor([tot_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        tot_ms = float(tt.item())
-        lt = torch.tensor([launches], dtype=torch.int64, device=dev)
-        dist.all_reduce(lt)
-        launches = int(lt.item())
-    value = T * world * args.steps / (tot_ms / 1e3)
+    tot_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    (tot_ms,) = ctx.max_over_ranks(tot_ms)
+    launches = ctx.sum_over_ranks(launches)
+    res = {"T": T, "scaling": scaling, "transport": transport, "value": T * world * steps / (tot_ms / 1e3),
+           "ms_per_step": tot_ms / steps, "launches": launches, "prof": prof, "clocks": clock_rec,
+           "graph": graph is not None, "weights": w, "x": x}
+    rows_local = int(counts.sum().item())
+
+    # ---- expert parallelism: every rank's output equals a single-GPU handle's
+    if want_parity and world > 1:
+        step()
+        torch.cuda.synchronize(dev)
+        ref = pkg.api.Handle(cfg.d_model, cfg.n_experts, cfg.top_k, cfg.expert_ff, cfg.dense_ff, dtype=cfg.dtype,
+                             device=ctx.local_rank, max_tokens=T)
+        ref.load_weights(w)
+        ref_out = torch.empty_like(out_dev)
+        ref.forward_device(x_dev.data_ptr(), ref_out.data_ptr(), T, sid)
+        ref.sync(sid)
+        same = bool(torch.equal(ref_out, out_dev))
+        ref.close()
+        del ref_out
+        res["ep_parity"] = ctx.all_ranks_true(same)
 
     # ---- end to end through the public API: pinned host in, pinned host out.
     # Serial: each step uploads x, runs the forward and downloads out on one
@@ -330,155 +388,114 @@ def run_ours(args):
     # i+1's upload and step i-1's download run on their own streams while
     # step i's forward runs, as a serving loop would; every step still moves
     # its own input up and its own output down inside the timed region.
-    e2e_serial_steps = max(3, min(args.steps, 20))
-    for _ in range(2):
-        x_dev.copy_(x_host, non_blocking=True)
-        step()
-        out_host.copy_(out_dev, non_blocking=True)
-    barrier()
-    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_serial_steps)]
-    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_serial_steps)]
-    for i in range(e2e_serial_steps):
-        flush.zero_()
-        e_s[i].record(stream)
-        x_dev.copy_(x_host, non_blocking=True)
-        step()
-        out_host.copy_(out_dev, non_blocking=True)
-        e_e[i].record(stream)
-    barrier()
-    serial_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(e_s, e_e))
+    if want_e2e:
+        out_host = torch.empty_like(x_host).pin_memory()
+        e2e_serial_steps = max(3, min(steps, 20))
+        for _ in range(2):
+            x_dev.copy_(x_host, non_blocking=True)
+            step()
+            out_host.copy_(out_dev, non_blocking=True)
+        ctx.barrier()
+        e_s = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_serial_steps)]
+        e_e = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_serial_steps)]
+        for i in range(e2e_serial_steps):
+            flush.zero_()
+            e_s[i].record(stream)
+            x_dev.copy_(x_host, non_blocking=True)
+            step()
+            out_host.copy_(out_dev, non_blocking=True)
+            e_e[i].record(stream)
+        ctx.barrier()
+        serial_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(e_s, e_e))
 
-    e2e_steps = max(4, min(args.steps, 100))
-    x_buf = [x_dev, torch.empty_like(x_dev)]
-    out_buf = [out_dev, torch.empty_like(out_dev)]
-    out_host_buf = [out_host, torch.empty_like(out_host).pin_memory()]
-    s_up, s_cmp, s_dn = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        e2e_steps = max(4, min(steps, 100))
+        x_buf = [x_dev, torch.empty_like(x_dev)]
+        out_buf = [out_dev, torch.empty_like(out_dev)]
+        out_host_buf = [out_host, torch.empty_like(out_host).pin_memory()]
+        s_up, s_cmp, s_dn = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
-    def fwd(b):
-        h.forward_device(x_buf[b].data_ptr(), out_buf[b].data_ptr(), T, s_cmp.cuda_stream,
-                         counts_ptr=counts.data_ptr())
+        def fwd(b):
+            h.forward_device(x_buf[b].data_ptr(), out_buf[b].data_ptr(), T, s_cmp.cuda_stream,
+                             counts_ptr=counts.data_ptr())
 
-    s_cmp.wait_stream(stream)
-    pgraphs = None
-    if graph is not None:
-        pgraphs = []
-        for b in range(2):
+        s_cmp.wait_stream(stream)
+        pgraphs = None
+        if graph is not None:
+            pgraphs = []
+            for b in range(2):
+                with torch.cuda.stream(s_cmp):
+                    fwd(b)
+                torch.cuda.synchronize(dev)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s_cmp):
+                    fwd(b)
+                pgraphs.append(g)
+        ctx.barrier()
+        ev_up = [torch.cuda.Event() for _ in range(e2e_steps)]
+        ev_cmp = [torch.cuda.Event() for _ in range(e2e_steps)]
+        ev_dn = [torch.cuda.Event() for _ in range(e2e_steps)]
+        p_start = torch.cuda.Event(enable_timing=True)
+        p_end = torch.cuda.Event(enable_timing=True)
+        p_start.record(s_up)
+        for i in range(e2e_steps):
+            b = i & 1
+            with torch.cuda.stream(s_up):
+                if i >= 2:
+                    s_up.wait_event(ev_cmp[i - 2])  # the forward that read x_buf[b] is done
+                x_buf[b].copy_(x_host, non_blocking=True)
+                ev_up[i].record(s_up)
             with torch.cuda.stream(s_cmp):
-                fwd(b)
-            torch.cuda.synchronize(dev)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=s_cmp):
-                fwd(b)
-            pgraphs.append(g)
-    barrier()
-    ev_up = [torch.cuda.Event() for _ in range(e2e_steps)]
-    ev_cmp = [torch.cuda.Event() for _ in range(e2e_steps)]
-    ev_dn = [torch.cuda.Event() for _ in range(e2e_steps)]
-    p_start = torch.cuda.Event(enable_timing=True)
-    p_end = torch.cuda.Event(enable_timing=True)
-    p_start.record(s_up)
-    for i in range(e2e_steps):
-        b = i & 1
-        with torch.cuda.stream(s_up):
-            if i >= 2:
-                s_up.wait_event(ev_cmp[i - 2])  # the forward that read x_buf[b] is done
-            x_buf[b].copy_(x_host, non_blocking=True)
-            ev_up[i].record(s_up)
-        with torch.cuda.stream(s_cmp):
-            s_cmp.wait_event(ev_up[i])
-            if i >= 2:
-                s_cmp.wait_event(ev_dn[i - 2])  # out_buf[b] has been downloaded
-            if pgraphs is not None:
-                pgraphs[b].replay()
-            else:
-                fwd(b)
-            ev_cmp[i].record(s_cmp)
-        with torch.cuda.stream(s_dn):
-            s_dn.wait_event(ev_cmp[i])
-            out_host_buf[b].copy_(out_buf[b], non_blocking=True)
-            ev_dn[i].record(s_dn)
-    p_end.record(s_dn)
-    barrier()
-    e2e_ms = p_start.elapsed_time(p_end)
-    del pgraphs
-    if world > 1:
-        tt = torch.tensor([e2e_ms, serial_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_ms, serial_ms = float(tt[0].item()), float(tt[1].item())
-    e2e = T * world * e2e_steps / (e2e_ms / 1e3)
-    e2e_serial = T * world * e2e_serial_steps / (serial_ms / 1e3)
-    io_bytes = int(x_host.numel() * x_host.element_size())
-
-    # ---- roofline of each kernel from the live per-launch events
-    pk, pk_kind = peaks()
-    rows_local = int(counts.sum().item()) if world == 1 else None
-    kern = kernel_rooflines(cfg, T, world, prof, pk, pk_kind, h, counts)
-
-    line = None
-    if rank == 0:
-        dom = kern.get("expert_gemm1")
-        roof = None
-        if dom:
-            roof = {"bound": "tensor", "kernel": "expert_gemm1 (grouped SwiGLU gate/up, tcgen05)",
-                    "achieved": dom["achieved"], "peak": dom["peak"], "unit": "TFLOP/s",
-                    "frac": dom["frac"],
-                    "traffic": GEMM1_DRAM_BYTES.get(cfg.name) if world == 1 else None,
-                    "traffic_unit": "bytes per launch (ncu capture)",
-                    "peak_source": f"bf16_tflops_sustained, {pk_kind}",
-                    "algorithmic_per_launch": dom["algorithmic_per_launch"],
-                    "avg_launch_ms": dom["avg_ms"]}
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": tot_ms / args.steps, "higher_is_better": True,
-            "scaling": scaling, "vs_baseline": None, "dtype": "bf16" if cfg.dtype == W.BF16 else "f32",
-            "data": "synthetic (seeded Philox; x = RMSNorm(N(0,1)), weights N(0,0.02), bias U(-0.1,0.1))",
-            "config": dict(config_dict(cfg, T, world, scaling), ep_transport=transport),
-            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes,
-                    "api": "noor_moe_forward (device mode) with pinned-host H2D/D2H in the timed region",
-                    "mode": f"pipelined over {e2e_steps} steps: step i+1's H2D and step i-1's D2H on their own "
-                            "streams overlap step i's forward (two device buffers)",
-                    "serial_value": e2e_serial},
-            "gpu_launches": launches,
-            "timing": ("CUDA-graph replay of one forward per step; per-kernel times from an uncaptured pass"
-                       if graph is not None else "plain calls; per-kernel events in the timed region"),
-            "roofline": roof,
-            "kernels": kern,
-            "clocks": clocks,
-        }
-        if world == 1 and not args.no_cpu_baseline:
-            n = cpu_sample_tokens(cfg)
-            xs = np.ascontiguousarray(x[:n])
-            v, cores, dt, blas = cpu_baseline(cfg, w, xs)
-            line["cpu_baseline"] = {
-                "value": v, "unit": UNIT, "cores": cores, "kind": "port",
-                "sample": f"{n} contiguous tokens of this batch through the oracle port of the reference "
-                          f"ParallelFFN/MoELayer forward ({'OpenBLAS sgemm' if blas else 'plain loops'}), "
-                          f"{dt:.1f} s"}
+                s_cmp.wait_event(ev_up[i])
+                if i >= 2:
+                    s_cmp.wait_event(ev_dn[i - 2])  # out_buf[b] has been downloaded
+                if pgraphs is not None:
+                    pgraphs[b].replay()
+                else:
+                    fwd(b)
+                ev_cmp[i].record(s_cmp)
+            with torch.cuda.stream(s_dn):
+                s_dn.wait_event(ev_cmp[i])
+                out_host_buf[b].copy_(out_buf[b], non_blocking=True)
+                ev_dn[i].record(s_dn)
+        p_end.record(s_dn)
+        ctx.barrier()
+        e2e_ms = p_start.elapsed_time(p_end)
+        del pgraphs
+        e2e_ms, serial_ms = ctx.max_over_ranks(e2e_ms, serial_ms)
+        io_bytes = int(x_host.numel() * x_host.element_size())
+        res["e2e"] = {"value": T * world * e2e_steps / (e2e_ms / 1e3), "unit": UNIT,
+                      "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes,
+                      "api": "noor_moe_forward (device mode) with pinned-host H2D/D2H in the timed region",
+                      "mode": f"pipelined over {e2e_steps} steps: step i+1's H2D and step i-1's D2H on their "
+                              "own streams overlap step i's forward (two device buffers)",
+                      "serial_value": T * world * e2e_serial_steps / (serial_ms / 1e3)}
+    del graph
     h.close()
     if comm:
         pkg.api.comm_destroy(comm)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if line is not None:
-        print(json.dumps(line), flush=True)
-    return 0
+    ctx.barrier()
+    res["rows_local"] = rows_local
+    return res
 
 
-def kernel_rooflines(cfg, T, world, prof, pk, pk_kind, h, counts):
+def kernel_rooflines(cfg, T, prof, pk, sm_mhz):
     """Per-kernel achieved rate from the live events: algorithmic FLOPs or
-    bytes per launch / average launch time."""
+    bytes per launch / average launch time.  Tensor-core kernels are divided
+    by the burst cuBLAS peak (they run for well under a millisecond at full
+    clock inside the step) and also given per GHz of the median SM clock."""
     d, E, k, ff, dff = cfg.d_model, cfg.n_experts, cfg.top_k, cfg.expert_ff, cfg.dense_ff
-    b = 2 if cfg.dtype == W.BF16 else 4
     R = T * k  # picks routed per rank (rows an expert GEMM processes per rank under uniform routing)
-    tf = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+    tf = pk.get("bf16_tflops", pk.get("bf16_tflops_sustained"))
     hbm = pk.get("hbm_gbs")
     by = W.algorithmic_bytes(cfg, T)
     spec = {
+        "router": ("hbm", by["router"]),
         "router_scores": ("hbm", by["router_scores"]),
         "router_topk": ("hbm", by["router_topk"]),
         "permute": ("hbm", by["permute"]),
         "combine": ("hbm", by["combine"]),
+        "norm_pre": ("hbm", by["norm_pre"]),
+        "norm_post": ("hbm", by["norm_post"]),
         "expert_gemm1": ("tensor", 2.0 * R * d * 2 * ff),
         "expert_gemm2": ("tensor", 2.0 * R * ff * d),
         "dense_gemm1": ("tensor", 2.0 * T * d * 2 * dff),
@@ -494,12 +511,98 @@ def kernel_rooflines(cfg, T, world, prof, pk, pk_kind, h, counts):
                 ach = amount / (avg / 1e3) / 1e12
                 ent.update(bound="tensor", achieved=ach, unit="TFLOP/s", peak=tf, frac=ach / tf,
                            algorithmic_per_launch=amount)
+                if sm_mhz:
+                    ent["tflops_per_ghz"] = ach / (sm_mhz / 1e3)
             else:
                 ach = amount / (avg / 1e3) / 1e9
                 ent.update(bound="hbm", achieved=ach, unit="GB/s", peak=hbm, frac=ach / hbm,
                            algorithmic_per_launch=amount)
         out[name] = ent
     return out
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    rank, local_rank, world = env_rank()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    ctx = Ctx(torch, dist, rank, local_rank, world, dev)
+    cfg = W.CONFIGS[args.config]
+    pk, pk_kind = peaks()
+
+    sampler = ClockSampler(local_rank)
+    r = measure_layer(ctx, cfg, args.steps, args.warmup, not args.no_graph, want_e2e=True,
+                      want_parity=True, clocks=sampler)
+    T = r["T"]
+    clocks = r["clocks"]
+    kern = kernel_rooflines(cfg, T, r["prof"], pk, clocks.get("sm_mhz"))
+
+    pro = None
+    if cfg.name != "pro" and not args.no_pro:
+        try:
+            pc = W.CONFIGS["pro"]
+            rp = measure_layer(ctx, pc, PRO_STEPS, args.warmup, not args.no_graph, want_e2e=False,
+                               want_parity=True)
+            pro = {"value": rp["value"], "unit": UNIT, "ms_per_step": rp["ms_per_step"], "steps": PRO_STEPS,
+                   "scaling": rp["scaling"], "config": config_dict(pc, rp["T"], world, rp["scaling"]),
+                   "ep_transport": rp["transport"], "gpu_launches": rp["launches"],
+                   "kernels": kernel_rooflines(pc, rp["T"], rp["prof"], pk, clocks.get("sm_mhz"))}
+            if "ep_parity" in rp:
+                pro["ep_parity"] = rp["ep_parity"]
+            del rp
+        except Exception as e:  # the headline line still prints
+            pro = {"error": f"{type(e).__name__}: {e}"}
+
+    line = None
+    if rank == 0:
+        dom = kern.get("expert_gemm1")
+        roof = None
+        if dom:
+            roof = {"bound": "tensor", "kernel": "expert_gemm1 (grouped SwiGLU gate/up, tcgen05)",
+                    "achieved": dom["achieved"], "peak": dom["peak"], "unit": "TFLOP/s",
+                    "frac": dom["frac"],
+                    "traffic": GEMM1_DRAM_BYTES.get(cfg.name) if world == 1 else None,
+                    "traffic_unit": "bytes per launch (ncu capture)",
+                    "peak_source": f"bf16_tflops (burst cuBLAS), {pk_kind}",
+                    "algorithmic_per_launch": dom["algorithmic_per_launch"],
+                    "avg_launch_ms": dom["avg_ms"],
+                    "tflops_per_ghz": dom.get("tflops_per_ghz")}
+        line = {
+            "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+            "scaling": r["scaling"], "vs_baseline": None, "dtype": "bf16" if cfg.dtype == W.BF16 else "f32",
+            "data": "synthetic (seeded Philox; x = RMSNorm(N(0,1)), weights N(0,0.02), bias U(-0.1,0.1))",
+            "config": config_dict(cfg, T, world, r["scaling"]),
+            "ep_transport": r["transport"],
+            "e2e": r["e2e"],
+            "gpu_launches": r["launches"],
+            "timing": ("CUDA-graph replay of one forward per step; per-kernel times from an uncaptured pass"
+                       if r["graph"] else "plain calls; per-kernel events in the timed region"),
+            "roofline": roof,
+            "kernels": kern,
+            "clocks": clocks,
+        }
+        if "ep_parity" in r:
+            line["ep_parity"] = r["ep_parity"]
+        if pro is not None:
+            line["pro"] = pro
+        if world == 1 and not args.no_cpu_baseline:
+            v, cores, dt, n, blas = cpu_baseline(cfg, r["weights"], r["x"])
+            line["cpu_baseline"] = {
+                "value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                "sample": f"oracle port of the reference ParallelFFN forward ({'OpenBLAS sgemm' if blas else 'plain loops'},"
+                          f" {cores} threads): dense GeGLU branch over all {T} tokens plus the per-token MoE loop"
+                          f" over {n} contiguous tokens, extrapolated to {T}; {dt:.1f} s of CPU time"}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
 
 
 def main():
@@ -510,6 +613,7 @@ def main():
     ap.add_argument("--config", default="edge", choices=sorted(W.CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-pro", action="store_true", help="skip the extra Pro-like pass")
     ap.add_argument("--no-graph", action="store_true", help="time plain calls instead of a captured forward")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":

@@ -289,9 +289,15 @@ NOOR_MOE_API int64_t noor_moe_launch_count(const noor_moe_handle* h);
  * per GPU; a call whose T, E, k would need more returns NOOR_MOE_ERR_INVALID
  * (E = 32, k = 4: about 450k tokens for BF16, 57k for F32, which also keeps
  * the f32 scores there).  The first call on each device looks up the array's
- * device address; make that first call before any stream capture.  Every call shares
- * the array and it keeps the last call's contents, so calls that can overlap
- * on the GPU (different streams, different host threads) race: serialise them. */
+ * device address; make that first call before any stream capture.  The
+ * address is kept for the life of the process, so do not call this again on a
+ * device after cudaDeviceReset.  Every call shares the array and it keeps the
+ * last call's contents, so calls that can overlap on the GPU (different
+ * streams, different host threads) race: serialise them.
+ * Errors found on the host return a status; a bounded wait on the device that
+ * gives up (BF16 router) cannot, since the call returns before the work runs:
+ * it is reported in the outputs instead, as every counts[e] == -1.  Check
+ * counts[0] >= 0 once the stream's work has completed. */
 NOOR_MOE_API int noor_moe_route_static(const void* x, const void* gate, const float* bias, const float* scales,
                                        int64_t T, int32_t d, int32_t E, int32_t top_k, int32_t dtype,
                                        int32_t* idx, float* w, int64_t* counts, void* stream);

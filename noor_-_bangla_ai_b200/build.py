@@ -5,6 +5,7 @@ next to this file; the CUDA runtime is linked statically, NCCL dynamically.
 """
 from __future__ import annotations
 
+import glob
 import os
 import subprocess
 import sys
@@ -14,7 +15,11 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libnoor_moe.so")
 SOURCES = ["noor_moe.cu"]
-HEADERS = ["nccl_dyn.h", "common.cuh", "tc_gemm.cuh", "simt_gemm.cuh", "router.cuh", "dispatch.cuh", "prepack.cuh"]
+
+
+def headers() -> list:
+    """Every header beside the sources: an edit to any of them rebuilds."""
+    return sorted(os.path.basename(p) for p in glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h")))
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -36,7 +41,7 @@ def stale() -> bool:
     if not os.path.exists(LIB):
         return True
     t = os.path.getmtime(LIB)
-    deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS]
+    deps = [os.path.join(CSRC, f) for f in SOURCES + headers()]
     deps.append(os.path.join(ROOT, "include", "noor_moe.h"))
     return any(os.path.getmtime(p) > t for p in deps if os.path.exists(p))
 

@@ -166,15 +166,25 @@ __device__ void scan_segments_block_staged(const int32_t* __restrict__ hist, int
   finish_segments(E, BM, s_seg, counts, seg_start, mtile_start, util, k);
 }
 
+// err (nullable): the router's device error word.  When it is set (a
+// bounded wait in the router gave up, so some picks are placeholders), every
+// count is written as -1 instead, so a caller without a handle sees the
+// failure in the counts it reads anyway.
 __global__ void __launch_bounds__(kScanThreads) scan_segments_kernel(const int32_t* __restrict__ hist, int32_t nblk,
                                                                      int32_t E, int32_t BM,
                                                                      int64_t* __restrict__ counts,
                                                                      int32_t* __restrict__ seg_start,
                                                                      int32_t* __restrict__ blk_base,
-                                                                     int32_t* __restrict__ mtile_start) {
+                                                                     int32_t* __restrict__ mtile_start,
+                                                                     const int* __restrict__ err = nullptr) {
   __shared__ int32_t s_warp[32];
   __shared__ int32_t s_seg[1025];
   scan_segments_block(hist, nblk, E, BM, counts, seg_start, blk_base, mtile_start, s_warp, s_seg);
+  if (err != nullptr) {
+    __syncthreads();
+    if (*reinterpret_cast<const volatile int*>(err) != 0)
+      for (int e = threadIdx.x; e < E; e += blockDim.x) counts[e] = -1;
+  }
 }
 
 // ------------------------------------------------------------------ permute

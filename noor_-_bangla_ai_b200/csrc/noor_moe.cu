@@ -1933,7 +1933,10 @@ void* g_scratch_addr[256] = {nullptr};  // device address of g_route_scratch, pe
 
 // Looks up the array's device address once per device, with that device
 // current.  In host code the name g_route_scratch is only a host-side stand-in,
-// never a usable device address.
+// never a usable device address.  The address is kept for the life of the
+// process: after cudaDeviceReset on a device the kept address no longer
+// names the array, so a process that resets a device must not call
+// noor_moe_route_static on it again.
 int route_scratch_address(int dev, void** out) {
   if (dev < 0 || dev >= 256) return fail(NOOR_MOE_ERR_INVALID, "device ordinal %d out of range", dev);
   std::lock_guard<std::mutex> lock(g_scratch_mu);
@@ -1967,8 +1970,10 @@ extern "C" int noor_moe_route_static(const void* x, const void* gate, const floa
   const int Epad = (E + 7) / 8 * 8;
   const int tpb = dtype == NOOR_DTYPE_BF16 ? router::kTcTPB : router::kTopkTPB;
   const int64_t nblk = (T + tpb - 1) / tpb;
-  // carve the array: ranks | block histograms | block bases | segment starts | tile starts | [scores]
-  const size_t off_lrank = 0;
+  // carve the array: error word | ranks | block histograms | block bases | segment starts | tile starts |
+  // [scores]
+  const size_t off_err = 0;
+  const size_t off_lrank = 256;
   const size_t off_hist = align256(off_lrank + (size_t)T * k * 4);
   const size_t off_base = align256(off_hist + (size_t)nblk * E * 4);
   const size_t off_seg = align256(off_base + (size_t)nblk * E * 4);
@@ -1986,6 +1991,11 @@ extern "C" int noor_moe_route_static(const void* x, const void* gate, const floa
   CKR(route_scratch_address(dev, &base));
   uint8_t* sb = static_cast<uint8_t*>(base);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The router records a bounded wait that gave up in the error word; the
+  // scan then writes every count as -1.  The word starts each call at zero
+  // (a memset allocates nothing).
+  int* err = reinterpret_cast<int*>(sb + off_err);
+  CK(cudaMemsetAsync(err, 0, sizeof(int), s));
   router::RouterOut ro{idx, w, reinterpret_cast<int32_t*>(sb + off_lrank), reinterpret_cast<int32_t*>(sb + off_hist)};
   float* scores = reinterpret_cast<float*>(sb + off_scores);
   const router::FusedScan nofs{nullptr, nullptr, nullptr, nullptr, nullptr, tc::BM, nullptr};
@@ -1995,7 +2005,7 @@ extern "C" int noor_moe_route_static(const void* x, const void* gate, const floa
     CUtensorMap tmx, tmg;
     CKR(encode_kmajor(&tmx, x, T, d, router::kTcTPB));
     CKR(encode_kmajor(&tmg, gate, Epad, d, router::tc_npad(E)));
-    CKR(launch_route_tc(nullptr, s, tmx, tmg, bias, scales, T, d, E, k, ro, nofs, nullptr));
+    CKR(launch_route_tc(nullptr, s, tmx, tmg, bias, scales, T, d, E, k, ro, nofs, err));
   } else {
     const int64_t n = T * E;
     router::route_f32_scores_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
@@ -2011,7 +2021,7 @@ extern "C" int noor_moe_route_static(const void* x, const void* gate, const floa
   dispatch::scan_segments_kernel<<<1, dispatch::kScanThreads, 0, s>>>(
       reinterpret_cast<const int32_t*>(sb + off_hist), (int32_t)nblk, E, tc::BM, counts,
       reinterpret_cast<int32_t*>(sb + off_seg), reinterpret_cast<int32_t*>(sb + off_base),
-      reinterpret_cast<int32_t*>(sb + off_mt));
+      reinterpret_cast<int32_t*>(sb + off_mt), err);
   CK(cudaGetLastError());
   return NOOR_MOE_OK;
 }

@@ -18,6 +18,8 @@ from __future__ import annotations
 
 import dataclasses
 import math
+import os
+from concurrent.futures import ThreadPoolExecutor
 from typing import Optional
 
 import numpy as np
@@ -45,6 +47,10 @@ class LayerConfig:
     hot_share: Optional[float] = None  # skewed routing: share of assignments to the hot experts
     hot_fraction: float = 0.25         # fraction of experts that are hot
     weight_std: float = 0.02
+    # Large layers: every expert matrix, dense matrix and 4096-row block of x
+    # has its own Philox stream (the base stream jumped), so the draws run on
+    # all host cores and do not depend on each other's order.
+    threaded_draw: bool = False
 
     def with_tokens(self, tokens: int) -> "LayerConfig":
         return dataclasses.replace(self, tokens=tokens)
@@ -72,8 +78,25 @@ CONFIGS = {
                                x_dist="rmsnorm", bias_dist="uniform0.1", hot_share=0.60),
     # Pro-like, expert-parallel across 1/2/4/8 GPUs.
     "pro": LayerConfig("pro", 131072, 3072, 64, 6, 1536, 3072, BF16, seed=1,
-                       x_dist="rmsnorm", bias_dist="uniform0.1"),
+                       x_dist="rmsnorm", bias_dist="uniform0.1", threaded_draw=True),
+    # The MoE layer of the Max-like stack (one of its 16 blocks): batch 8 x
+    # seq 4096 tokens, d_model 4096, 128 experts top-8.
+    "max_layer": LayerConfig("max_layer", 32768, 4096, 128, 8, 1536, 4096, BF16, seed=2,
+                             x_dist="rmsnorm", bias_dist="uniform0.1", threaded_draw=True),
 }
+
+TOKEN_BLOCK = 4096  # rows of x per Philox stream under threaded_draw
+
+
+def _pool_map(fn, items):
+    items = list(items)
+    with ThreadPoolExecutor(max_workers=max(1, min(len(items), os.cpu_count() or 1))) as ex:
+        return list(ex.map(fn, items))
+
+
+def _stream(seed: int, i: int) -> np.random.Generator:
+    """Stream i of the threaded draws: the base Philox stream jumped i + 1 times."""
+    return np.random.Generator(np.random.Philox(seed).jumped(i + 1))
 
 
 def bf16_round(a: np.ndarray) -> np.ndarray:
@@ -136,9 +159,19 @@ def _topk_share(x: np.ndarray, gate: np.ndarray, bias: np.ndarray, k: int, hot: 
     return float(np.isin(top, hot).mean())
 
 
+def _fill_normal(out: np.ndarray, rng: np.random.Generator, std: float, bf16: bool) -> None:
+    rng.standard_normal(out=out, dtype=np.float32)
+    out *= np.float32(std)
+    if bf16:
+        out[...] = bf16_round(out)
+
+
 def make_weights(cfg: LayerConfig, rng: Optional[np.random.Generator] = None) -> LayerWeights:
     """Draw the layer's weights.  Order of draws: router gate, bias, experts
-    (gate, up, down per expert), shared expert, dense branch."""
+    (gate, up, down per expert), shared expert, dense branch.  Under
+    cfg.threaded_draw the gate and bias come from the base stream and every
+    larger matrix from its own stream: expert e's gate, up and down from
+    streams 3e, 3e+1, 3e+2, then the dense and shared matrices."""
     if rng is None:
         rng = np.random.Generator(np.random.Philox(cfg.seed))
     d, E, ff, dff, std = cfg.d_model, cfg.n_experts, cfg.expert_ff, cfg.dense_ff, cfg.weight_std
@@ -151,14 +184,30 @@ def make_weights(cfg: LayerConfig, rng: Optional[np.random.Generator] = None) ->
     w_gate = np.empty((E, d, ff), np.float32)
     w_up = np.empty((E, d, ff), np.float32)
     w_down = np.empty((E, ff, d), np.float32)
-    for e in range(E):
-        w_gate[e] = _normal(rng, (d, ff), std)
-        w_up[e] = _normal(rng, (d, ff), std)
-        w_down[e] = _normal(rng, (ff, d), std)
     sg = su = sd = None
-    if cfg.has_shared:
-        sg, su, sd = _normal(rng, (d, ff), std), _normal(rng, (d, ff), std), _normal(rng, (ff, d), std)
-    dg, du, dd = _normal(rng, (d, dff), std), _normal(rng, (d, dff), std), _normal(rng, (dff, d), std)
+    if cfg.threaded_draw:
+        bf = cfg.dtype == BF16
+        dg, du, dd = (np.empty((d, dff), np.float32), np.empty((d, dff), np.float32),
+                      np.empty((dff, d), np.float32))
+        jobs = []
+        for e in range(E):
+            jobs += [(w_gate[e], 3 * e), (w_up[e], 3 * e + 1), (w_down[e], 3 * e + 2)]
+        jobs += [(dg, 3 * E), (du, 3 * E + 1), (dd, 3 * E + 2)]
+        if cfg.has_shared:
+            sg, su, sd = np.empty((d, ff), np.float32), np.empty((d, ff), np.float32), np.empty((ff, d), np.float32)
+            jobs += [(sg, 3 * E + 3), (su, 3 * E + 4), (sd, 3 * E + 5)]
+        _pool_map(lambda j: _fill_normal(j[0], _stream(cfg.seed, j[1]), std, bf), jobs)
+        rounded = {"w_gate", "w_up", "w_down", "dense_gate", "dense_up", "dense_down", "shared_gate",
+                   "shared_up", "shared_down"} if bf else set()
+    else:
+        for e in range(E):
+            w_gate[e] = _normal(rng, (d, ff), std)
+            w_up[e] = _normal(rng, (d, ff), std)
+            w_down[e] = _normal(rng, (ff, d), std)
+        if cfg.has_shared:
+            sg, su, sd = _normal(rng, (d, ff), std), _normal(rng, (d, ff), std), _normal(rng, (ff, d), std)
+        dg, du, dd = _normal(rng, (d, dff), std), _normal(rng, (d, dff), std), _normal(rng, (dff, d), std)
+        rounded = set()
     w = LayerWeights(gate, bias, scales, w_gate, w_up, w_down, dg, du, dd, sg, su, sd)
     if cfg.hot_share is not None:
         _skew_router(cfg, w)
@@ -166,7 +215,7 @@ def make_weights(cfg: LayerConfig, rng: Optional[np.random.Generator] = None) ->
         for f in ("gate", "w_gate", "w_up", "w_down", "dense_gate", "dense_up", "dense_down",
                   "shared_gate", "shared_up", "shared_down"):
             v = getattr(w, f)
-            if v is not None:
+            if v is not None and f not in rounded:
                 setattr(w, f, bf16_round(v))
     return w
 
@@ -203,17 +252,35 @@ def _skew_router(cfg: LayerConfig, w: LayerWeights) -> None:
                                        cfg.top_k, hot)
 
 
-def make_tokens(cfg: LayerConfig, seed_offset: int = 1, tokens: Optional[int] = None) -> np.ndarray:
-    """Draw x [T, d] (f32; BF16-rounded for BF16 layers) from its own Philox
-    stream (seed + seed_offset), so token count does not change the weights."""
-    T = cfg.tokens if tokens is None else tokens
-    rng = np.random.Generator(np.random.Philox(cfg.seed + seed_offset))
-    x = rng.standard_normal(size=(T, cfg.d_model), dtype=np.float32)
+def _token_rows(cfg: LayerConfig, x: np.ndarray) -> np.ndarray:
     if cfg.x_dist == "rmsnorm":
         x = rms_norm_rows(x)
     if cfg.dtype == BF16:
         x = bf16_round(x)
-    return np.ascontiguousarray(x)
+    return x
+
+
+def make_tokens(cfg: LayerConfig, seed_offset: int = 1, tokens: Optional[int] = None) -> np.ndarray:
+    """Draw x [T, d] (f32; BF16-rounded for BF16 layers) from its own Philox
+    stream (seed + seed_offset), so token count does not change the weights.
+    Under cfg.threaded_draw every TOKEN_BLOCK rows come from their own stream
+    (drawn on all host cores); the first n rows are the same for any T >= n
+    either way."""
+    T = cfg.tokens if tokens is None else tokens
+    if cfg.threaded_draw:
+        x = np.empty((T, cfg.d_model), np.float32)
+
+        def block(b):
+            r0, r1 = b * TOKEN_BLOCK, min(T, (b + 1) * TOKEN_BLOCK)
+            part = _stream(cfg.seed + seed_offset, b).standard_normal(size=(TOKEN_BLOCK, cfg.d_model),
+                                                                      dtype=np.float32)[: r1 - r0]
+            x[r0:r1] = _token_rows(cfg, part)
+
+        _pool_map(block, range((T + TOKEN_BLOCK - 1) // TOKEN_BLOCK))
+        return x
+    rng = np.random.Generator(np.random.Philox(cfg.seed + seed_offset))
+    x = rng.standard_normal(size=(T, cfg.d_model), dtype=np.float32)
+    return np.ascontiguousarray(_token_rows(cfg, x))
 
 
 def algorithmic_bytes(cfg: LayerConfig, tokens: int) -> dict:
@@ -223,6 +290,9 @@ def algorithmic_bytes(cfg: LayerConfig, tokens: int) -> dict:
     d, E, k = cfg.d_model, cfg.n_experts, cfg.top_k
     T = tokens
     return {
+        # BF16 router (one kernel): x once, gate once, (index, weight) per
+        # pick, the E counts
+        "router": T * d * b + d * E * b + T * k * 8 + 8 * E,
         # x once, router gate once, f32 scores written
         "router_scores": T * d * b + d * E * b + T * E * 4,
         # scores read; index, weight and rank per pick written
@@ -231,6 +301,10 @@ def algorithmic_bytes(cfg: LayerConfig, tokens: int) -> dict:
         "permute": T * d * b + T * k * d * b + 8 * T * k,
         # k expert rows gathered, out written, (index, weight) per pick
         "combine": T * k * d * b + T * d * b + 8 * T * k,
+        # sandwich norm: pre reads h and writes the normalised input; post
+        # reads the layer output and the residual and writes the sublayer output
+        "norm_pre": 2 * T * d * b,
+        "norm_post": 3 * T * d * b,
     }
 
 

@@ -32,6 +32,8 @@ def _run(n, *extra):
     ("--transport", "nccl"),                        # the NCCL all-to-all-v exchange
     ("--transport", "nccl", "--uneven"),
     ("--config", "proxy_tiny", "--tokens", "777"),  # F32 layer (NCCL exchange)
+    ("--config", "pro", "--tokens", "4000", "--transport", "peer"),        # E = 64, k = 6 over 2/4/8 owners
+    ("--config", "max_layer", "--tokens", "2000", "--transport", "peer"),  # E = 128, k = 8
 ])
 def test_expert_parallel_matches_single_gpu(extra):
     n = min(_ngpu(), 8)

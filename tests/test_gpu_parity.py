@@ -136,8 +136,13 @@ def _sampled_rows(T, n, seed=0):
     return np.sort(rng.choice(T, size=min(n, T), replace=False))
 
 
-@pytest.mark.parametrize("name,tokens,sample", [("edge", None, 48), ("edge_skewed", None, 32), ("pro", 8192, 16)])
+@pytest.mark.parametrize("name,tokens,sample", [("edge", None, 48), ("edge_skewed", None, 32), ("pro", None, 32),
+                                                ("max_layer", None, 32)])
 def test_bf16_config_sampled(pkg, oracle, name, tokens, sample):
+    """Every config at its full size: the router on every token against the
+    oracle, sampled output rows against the oracle's forward of those rows.
+    max_layer (E = 128, k = 8) sits at the BF16 router's limits: 128 TMEM
+    columns read in four 32-column loads, and the largest top-k."""
     cfg = pkg.workloads.CONFIGS[name]
     if tokens is not None:
         cfg = cfg.with_tokens(tokens)

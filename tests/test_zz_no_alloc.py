@@ -5,9 +5,12 @@ is not allowed while a stream is captured) and hosts that hand all device
 memory to their own pool at start-up.  noor_moe_route_static serves them by
 running the router out of one fixed device array in the library.  This file
 checks, through the C ABI, that two calls in a row give the same picks,
-weights and counts as the handle-based noor_moe_route, that the free device
-memory does not change, and that a batch too big for the array is refused.
-It is named so that pytest collects it last.
+weights and counts as the handle-based noor_moe_route and as the CPU oracle's
+router (picks and counts exact up to score ties, the parity tests' rule),
+that no count comes back as -1 (the entry point's in-band report of a device
+wait that gave up), that the free device memory does not change, and that a
+batch too big for the array is refused.  It is named so that pytest collects
+it last.
 """
 import numpy as np
 import pytest
@@ -59,8 +62,20 @@ def _route_static(pkg, cfg, xd, gate, bias, scales, T):
     return idx.cpu().numpy(), wt.cpu().numpy(), counts.cpu().numpy(), (free_before, free_after)
 
 
+def _check_oracle(pkg, oracle, cfg, w, x, idx, wt, counts):
+    """Picks, weights and counts against the oracle's router on the same tokens."""
+    W = pkg.workloads
+    ridx, _rw, rcounts, rscores = oracle.route(x, w.gate, w.bias, w.scales, cfg.top_k, want_scores=True)
+    tau = parity.TAU_BF16 if cfg.dtype == W.BF16 else parity.TAU_F32
+    rep = parity.compare_routing(idx, wt, ridx, rscores, w.scales, tau)
+    assert rep["unexplained"] == [], rep
+    assert rep["max_score_err"] <= tau / 2, rep
+    assert rep["tokens_differ"] <= max(2, x.shape[0] // 500), rep
+    assert parity.counts_consistent(counts, rcounts, rep["tokens_differ"], idx.shape[1]), (counts, rcounts)
+
+
 @pytest.mark.parametrize("name", ["edge", "proxy_tiny"])
-def test_route_static_matches_route_twice(pkg, name):
+def test_route_static_matches_route_twice(pkg, oracle, name):
     import torch
     W = pkg.workloads
     cfg = W.CONFIGS[name].with_tokens(3000)
@@ -72,17 +87,21 @@ def test_route_static_matches_route_twice(pkg, name):
     # first call: all 3000 tokens
     idx_ref, w_ref, c_ref = h.route_host(xin)
     idx, wt, counts, mem1 = _route_static(pkg, cfg, xd, gate, bias, scales, cfg.tokens)
+    assert (counts >= 0).all(), counts  # -1 would report a device wait that gave up
     assert np.array_equal(idx, idx_ref)
     np.testing.assert_allclose(wt, w_ref, rtol=0, atol=tol)
     assert np.array_equal(counts, c_ref)
+    _check_oracle(pkg, oracle, cfg, w, x, idx, wt, counts)
     # second call right after, on a shorter batch: the array still holds the
     # first call's contents and must not leak into the result
     lo, hi = 1000, 1777
     idx_ref2, w_ref2, c_ref2 = h.route_host(np.ascontiguousarray(xin[lo:hi]))
     idx2, wt2, counts2, mem2 = _route_static(pkg, cfg, xd[lo:hi].contiguous(), gate, bias, scales, hi - lo)
+    assert (counts2 >= 0).all(), counts2
     assert np.array_equal(idx2, idx_ref2)
     np.testing.assert_allclose(wt2, w_ref2, rtol=0, atol=tol)
     assert np.array_equal(counts2, c_ref2)
+    _check_oracle(pkg, oracle, cfg, w, x[lo:hi], idx2, wt2, counts2)
     assert int(counts2.sum()) == (hi - lo) * min(cfg.top_k, cfg.n_experts)
     assert mem1[0] == mem1[1] and mem2[0] == mem2[1]  # no device allocation inside the call
     h.close()
