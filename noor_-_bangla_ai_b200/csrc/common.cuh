@@ -84,7 +84,10 @@ __device__ __forceinline__ TileCoord decode_tile(const GroupTable& gt, int32_t t
 // shared-memory latency, not a chain of global loads; larger tables stay in
 // global memory.  All threads of the block call it; it ends with
 // __syncthreads().
-constexpr int kSmemGroups = 1024;
+// A layer has at most 256 experts and every group table (one GPU: E
+// experts; expert parallel: G*E/G = E (source rank, local expert) groups) has
+// at most E groups.
+constexpr int kSmemGroups = 256;
 __device__ __forceinline__ GroupTable stage_group_table(const GroupTable& gt, int32_t* s_tab) {
   GroupTable out = gt;
   if (gt.dense_rows < 0 && gt.G <= kSmemGroups) {

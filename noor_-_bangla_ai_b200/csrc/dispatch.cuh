@@ -191,16 +191,18 @@ __global__ void __launch_bounds__(kScanThreads) scan_segments_kernel(const int32
 
 // Each warp takes tokens in a grid-stride loop: it reads the token's row once
 // (up to 4 KB in one batch of 16-byte loads) and writes it to the row of each
-// of its k picks, recording that row in dst_row[t, slot].  Launched either
-// with a block per 4 tokens, or persistent with one 4-warp block per SM
-// (48 registers a thread) beside a tensor-core GEMM that holds the rest of
-// each SM.
+// of its k picks, recording that row in dst_row[t, slot] and, when ymap is
+// given, the inverse ymap[row] = t*k + slot (where the expert down
+// projection puts that row's output: token-major, so the combine reads each
+// token's k rows side by side).  Launched either with a block per 4 tokens,
+// or persistent with one 4-warp block per SM (48 registers a thread) beside a
+// tensor-core GEMM that holds the rest of each SM.
 constexpr int kPermuteWarps = 4;
 
 __global__ void __launch_bounds__(kPermuteWarps * 32) permute_rows_kernel(
     const uint8_t* __restrict__ x, int32_t row_bytes, int32_t T, int32_t k, int32_t nblk, int32_t tpb,
     const int32_t* __restrict__ idx, const int32_t* __restrict__ lrank, const int32_t* __restrict__ blk_base,
-    uint8_t* __restrict__ xp, int32_t* __restrict__ dst_row) {
+    uint8_t* __restrict__ xp, int32_t* __restrict__ dst_row, int32_t* __restrict__ ymap) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nvec = row_bytes >> 4;
   constexpr int U = 8;
@@ -213,6 +215,7 @@ __global__ void __launch_bounds__(kPermuteWarps * 32) permute_rows_kernel(
         const int32_t e = __ldg(idx + (int64_t)t * k + i);
         dst[i] = __ldg(bb + (int64_t)e * nblk) + __ldg(lrank + (int64_t)t * k + i);
         if (lane == 0) dst_row[(int64_t)t * k + i] = dst[i];
+        if (lane == 1 && ymap != nullptr) ymap[dst[i]] = t * k + i;
       }
     }
     const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)t * row_bytes);
@@ -240,7 +243,8 @@ __global__ void __launch_bounds__(kPermuteWarps * 32) permute_rows_kernel(
 // with the sum taken in rank order starting from zero and every multiply and
 // add rounded separately (moe.rs:159-173, parallel_ffn.rs:32-35).  Without a
 // dense branch the result is the MoE sum alone (MoELayer::forward).
-// YT / OUT: bf16 or float.  dense and shared are f32 (nullable).
+// YT / OUT: bf16 or float.  dense and shared are f32 (nullable).  dst_row
+// null: y is token-major, pick (t, i) at row t*k + i.
 template <typename T_>
 struct Vec8;
 template <>
@@ -283,7 +287,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32) combine_kernel(
 #pragma unroll
   for (int i = 0; i < 8; ++i)
     if (i < k) {
-      rows[i] = __ldg(dst_row + (int64_t)t * k + i);
+      rows[i] = dst_row != nullptr ? __ldg(dst_row + (int64_t)t * k + i) : t * k + i;
       w[i] = __ldg(wts + (int64_t)t * k + i);
     }
   const float inv_sqrt2 = 0x1.6a09e6p-1f;  // 1.0f32 / 2.0f32.sqrt() = 0.70710677

@@ -214,6 +214,7 @@ struct noor_moe_handle {
   DevBuf scores;
   DevBuf scan_done;  // zeroed counter for the router's fused scan
   DevBuf xp, h, y, xrecv, ysend;
+  DevBuf ymap;  // [picks] token-major output row of each expert-ordered row (BF16, one GPU)
   DevBuf dense_h, dense_out, shared_h, shared_out;
   DevBuf grp_row, grp_mtile, grp_widx, cnt_recv;
   // expert parallelism over peer memory (BF16 layers whose GPUs reach each
@@ -222,6 +223,7 @@ struct noor_moe_handle {
   bool peer = false;
   int64_t capP = 0;                 // tokens per rank (the largest max_tokens of all ranks)
   DevBuf pxrecv, py, psync;         // receive rows | returned expert outputs | flags + counts
+  DevBuf prowmap;                   // [receive rows] sender's token-major output row of each received row
   DevBuf pseq, pstatus, dest_base, grp_orank, grp_oshift;
   noor::peer::Peers peers{};
   void* peer_y[noor::peer::kMaxRanks] = {};
@@ -436,6 +438,7 @@ int ensure_workspace(noor_moe_handle* h, int64_t T) {
     CKR(h->xp.ensure(Rl * d * b));
     CKR(h->y.ensure(Rr * d * b));
   }
+  if (h->bf16 && h->G == 1) CKR(h->ymap.ensure(Rl * 4));
   if (h->G > 1 && !h->peer) {
     CKR(h->xrecv.ensure(Rr * d * b));
     CKR(h->ysend.ensure(Rl * d * b));
@@ -496,21 +499,27 @@ struct CombineArgs {
   const float* wts;
   const float* shared;
   int32_t k;
+  bool y_token_major;  // y row of pick (t, i) is t*k + i (dst_row unused)
 };
 
-// Expert parallelism over peer memory: the store epilogue sends group g's
-// rows to rank rank[g]'s buffer bases[rank[g]] at row + shift[g].
+// Where the plain-store epilogue puts its rows.  Expert parallelism over
+// peer memory: group g's rows go to rank rank[g]'s buffer bases[rank[g]]
+// (rank null: the GEMM's own C).  Row r goes to rowmap[r] when rowmap is set
+// (token-major y), else to r + shift[g].
 struct PeerOut {
   const int32_t* rank;
   const int32_t* shift;
   void* const* bases;
+  const int32_t* rowmap;
 };
 
 void set_peer_out(tc::Params& p, const PeerOut* po) {
   if (!po) return;
   p.out_rank = po->rank;
   p.out_shift = po->shift;
-  for (int r = 0; r < noor::peer::kMaxRanks; ++r) p.out_peer[r] = po->bases[r];
+  if (po->bases)
+    for (int r = 0; r < noor::peer::kMaxRanks; ++r) p.out_peer[r] = po->bases[r];
+  p.out_rowmap = po->rowmap;
 }
 
 // Raise a kernel's dynamic shared-memory limit to at least `bytes`.  Up to
@@ -564,6 +573,7 @@ int launch_tc(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& t
     p.wts = comb->wts;
     p.shared = comb->shared;
     p.k = comb->k;
+    p.y_token_major = comb->y_token_major ? 1 : 0;
   }
   set_peer_out(p, po);
   const int64_t tiles = std::max<int64_t>(1, max_mtiles * p.n_tiles);
@@ -591,6 +601,7 @@ int launch_tc2(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& 
     p.wts = comb->wts;
     p.shared = comb->shared;
     p.k = comb->k;
+    p.y_token_major = comb->y_token_major ? 1 : 0;
   }
   set_peer_out(p, po);
   const int64_t tiles = std::max<int64_t>(1, max_tiles * p.n_tiles);
@@ -872,8 +883,8 @@ int allgather_bytes(noor_moe_handle* h, const void* mine, void* all, size_t byte
 void peer_release(noor_moe_handle* h) {
   for (void* p : h->ipc_opened) cudaIpcCloseMemHandle(p);
   h->ipc_opened.clear();
-  DevBuf* bufs[] = {&h->pxrecv, &h->py, &h->psync, &h->pseq, &h->pstatus, &h->dest_base, &h->grp_orank,
-                    &h->grp_oshift};
+  DevBuf* bufs[] = {&h->pxrecv, &h->py, &h->psync, &h->prowmap, &h->pseq, &h->pstatus, &h->dest_base,
+                    &h->grp_orank, &h->grp_oshift};
   for (DevBuf* b : bufs) b->release();
   h->peer = false;
 }
@@ -930,6 +941,7 @@ int peer_setup(noor_moe_handle* h) {
   auto alloc = [&]() -> int {
     CKR(h->pxrecv.ensure(cap_rows * d * 2));
     CKR(h->py.ensure(capP * k * d * 2));
+    CKR(h->prowmap.ensure(cap_rows * 4));
     CKR(h->psync.ensure(round_up(P::kCountsOff + (int64_t)G * E * 8, 4096)));
     CKR(h->pseq.ensure(8));
     CKR(h->pstatus.ensure(4));
@@ -957,19 +969,21 @@ int peer_setup(noor_moe_handle* h) {
   // exchange the buffers' IPC handles (and raw addresses, for ranks that
   // share this process) and map the other ranks' buffers
   struct Handles {
-    cudaIpcMemHandle_t x, y, sy;
-    uint64_t px, py, ps;
+    cudaIpcMemHandle_t x, y, sy, rm;
+    uint64_t px, py, ps, prm;
   };
   Handles hm{};
   int64_t ok3 = 1;
   if (cudaIpcGetMemHandle(&hm.x, h->pxrecv.p) != cudaSuccess || cudaIpcGetMemHandle(&hm.y, h->py.p) != cudaSuccess ||
-      cudaIpcGetMemHandle(&hm.sy, h->psync.p) != cudaSuccess) {
+      cudaIpcGetMemHandle(&hm.sy, h->psync.p) != cudaSuccess ||
+      cudaIpcGetMemHandle(&hm.rm, h->prowmap.p) != cudaSuccess) {
     cudaGetLastError();
     ok3 = 0;
   }
   hm.px = reinterpret_cast<uint64_t>(h->pxrecv.p);
   hm.py = reinterpret_cast<uint64_t>(h->py.p);
   hm.ps = reinterpret_cast<uint64_t>(h->psync.p);
+  hm.prm = reinterpret_cast<uint64_t>(h->prowmap.p);
   std::vector<Handles> hs(G);
   CKR(allgather_bytes(h, &hm, hs.data(), sizeof(Handles)));
   P::Peers peers{};
@@ -979,7 +993,7 @@ int peer_setup(noor_moe_handle* h) {
   const int64_t tms = tenv ? std::max<int64_t>(1, std::atoll(tenv)) : 10000;
   peers.timeout_ns = tms * 1000000LL;
   for (int r = 0; r < G && ok3; ++r) {
-    void *px = nullptr, *py = nullptr, *ps = nullptr;
+    void *px = nullptr, *py = nullptr, *ps = nullptr, *prm = nullptr;
     if (r == me || all[r].pid == mine.pid) {
       if (r != me) {
         cudaError_t e = cudaDeviceEnablePeerAccess(ord[r], 0);
@@ -989,10 +1003,11 @@ int peer_setup(noor_moe_handle* h) {
       px = reinterpret_cast<void*>(hs[r].px);
       py = reinterpret_cast<void*>(hs[r].py);
       ps = reinterpret_cast<void*>(hs[r].ps);
+      prm = reinterpret_cast<void*>(hs[r].prm);
     } else {
-      void* m[3] = {nullptr, nullptr, nullptr};
-      const cudaIpcMemHandle_t* src[3] = {&hs[r].x, &hs[r].y, &hs[r].sy};
-      for (int i = 0; i < 3; ++i) {
+      void* m[4] = {nullptr, nullptr, nullptr, nullptr};
+      const cudaIpcMemHandle_t* src[4] = {&hs[r].x, &hs[r].y, &hs[r].sy, &hs[r].rm};
+      for (int i = 0; i < 4; ++i) {
         if (cudaIpcOpenMemHandle(&m[i], *src[i], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
           cudaGetLastError();
           ok3 = 0;
@@ -1003,9 +1018,11 @@ int peer_setup(noor_moe_handle* h) {
       px = m[0];
       py = m[1];
       ps = m[2];
+      prm = m[3];
     }
     peers.xrecv[r] = static_cast<uint8_t*>(px);
     peers.sync[r] = static_cast<uint8_t*>(ps);
+    peers.rowmap[r] = static_cast<int32_t*>(prm);
     h->peer_y[r] = py;
   }
   CKR(allreduce_min(h, &ok3));
@@ -1121,7 +1138,7 @@ int run_forward_peer(noor_moe_handle* h, cudaStream_t s, const void* x, const CU
   gt.G = E;
   gt.dense_rows = -1;
   const int64_t max_mtiles = (cap_rows + h->tile_m - 1) / h->tile_m + E;
-  const PeerOut pout{h->grp_orank.as<int32_t>(), h->grp_oshift.as<int32_t>(), h->peer_y};
+  const PeerOut pout{h->grp_orank.as<int32_t>(), h->grp_oshift.as<int32_t>(), h->peer_y, h->prowmap.as<int32_t>()};
   CKR(launch_gemm<tc::EPI_SWIGLU_BF16>(h, s, K_EXPERT_GEMM1, h->tm_pxrecv, h->tm_w1, gt, 2 * h->ff, d, h->h.p, h->ff,
                                        max_mtiles));
   CKR(launch_gemm<tc::EPI_STORE_BF16>(h, s, K_EXPERT_GEMM2, h->tm_h, h->tm_w2, gt, d, h->ff, nullptr, d, max_mtiles,
@@ -1131,14 +1148,13 @@ int run_forward_peer(noor_moe_handle* h, cudaStream_t s, const void* x, const CU
   if (fork) CK(cudaStreamWaitEvent(s, h->ev_join, 0));
   const float* shared_out = h->has_shared ? h->shared_out.as<float>() : nullptr;
   if (h->has_dense) {
-    const CombineArgs comb{h->py.p, h->dst_row.as<int32_t>(), h->wts.as<float>(), shared_out, k};
+    const CombineArgs comb{h->py.p, h->dst_row.as<int32_t>(), h->wts.as<float>(), shared_out, k, true};
     return glu_down(h, s, dense, out, &comb);
   }
   return launch(h, s, K_COMBINE, [&] {
     const unsigned grid = (unsigned)((T + dispatch::kCombineWarps - 1) / dispatch::kCombineWarps);
     dispatch::combine_kernel<bf16, bf16><<<grid, dispatch::kCombineWarps * 32, 0, s>>>(
-        h->py.as<bf16>(), h->dst_row.as<int32_t>(), h->wts.as<float>(), nullptr, shared_out, (int32_t)T, d, k,
-        (bf16*)out);
+        h->py.as<bf16>(), nullptr, h->wts.as<float>(), nullptr, shared_out, (int32_t)T, d, k, (bf16*)out);
   });
 }
 
@@ -1160,6 +1176,11 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
   const GluFfn shared{K_SHARED_GEMM1, K_SHARED_GEMM2, tmx, x, T, h->ff, true, &h->tm_sw1, &h->tm_sw2, &h->tm_sh,
                       h->sg32.as<float>(), h->su32.as<float>(), h->sd32.as<float>(), h->shared_h.p};
   const bool fuse_combine = h->bf16 && h->has_dense;
+  // BF16 on one GPU: the expert down projection writes y token-major (row
+  // t*k + slot, through the permute's row map), so the combine reads each
+  // token's k rows side by side.  The NCCL exchange returns rows in the
+  // expert order and the combine gathers them through dst_row.
+  const bool token_major = h->bf16 && h->G == 1;
   // The side branches (dense up projection, shared expert) run on a second
   // stream under the NCCL exchange, from the start, beside the transfers.  On
   // one GPU they run in line after the expert GEMMs unless kForkSideSingle.
@@ -1203,8 +1224,8 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
       const unsigned grid = (unsigned)(side ? std::min<int64_t>(blocks, h->num_sms) : blocks);
       dispatch::permute_rows_kernel<<<grid, dispatch::kPermuteWarps * 32, 0, s>>>(
           static_cast<const uint8_t*>(x), (int32_t)(d * b), (int32_t)T, k, (int32_t)((T + tpb - 1) / tpb), tpb,
-          h->idx.as<int32_t>(),
-          h->lrank.as<int32_t>(), h->blk_base.as<int32_t>(), h->xp.as<uint8_t>(), h->dst_row.as<int32_t>());
+          h->idx.as<int32_t>(), h->lrank.as<int32_t>(), h->blk_base.as<int32_t>(), h->xp.as<uint8_t>(),
+          h->dst_row.as<int32_t>(), token_major ? h->ymap.as<int32_t>() : nullptr);
     }));
   }
 
@@ -1245,8 +1266,9 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
     if (h->bf16) {
       CKR(launch_gemm<tc::EPI_SWIGLU_BF16>(h, s, K_EXPERT_GEMM1, *tA, h->tm_w1, gt, 2 * h->ff, d, h->h.p, h->ff,
                                            max_mtiles));
+      const PeerOut ytm{nullptr, nullptr, nullptr, h->ymap.as<int32_t>()};
       CKR(launch_gemm<tc::EPI_STORE_BF16>(h, s, K_EXPERT_GEMM2, h->tm_h, h->tm_w2, gt, d, h->ff, h->y.p, d,
-                                          max_mtiles));
+                                          max_mtiles, nullptr, token_major ? &ytm : nullptr));
     } else {
       const int64_t ffd = (int64_t)d * h->ff;
       CKR((launch_simt<simt::EPI_SWIGLU>(h, s, K_EXPERT_GEMM1, gt, (const float*)A32, d, h->wg32.as<float>(),
@@ -1262,7 +1284,7 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
   if (T == 0) return NOOR_MOE_OK;
   const float* shared_out = h->has_shared ? h->shared_out.as<float>() : nullptr;
   if (fuse_combine) {
-    const CombineArgs comb{ybuf, h->dst_row.as<int32_t>(), h->wts.as<float>(), shared_out, k};
+    const CombineArgs comb{ybuf, h->dst_row.as<int32_t>(), h->wts.as<float>(), shared_out, k, token_major};
     return glu_down(h, s, dense, out, &comb);
   }
   return launch(h, s, K_COMBINE, [&] {
@@ -1270,8 +1292,8 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
     const float* dense_out = h->has_dense ? h->dense_out.as<float>() : nullptr;
     if (h->bf16)
       dispatch::combine_kernel<bf16, bf16><<<grid, dispatch::kCombineWarps * 32, 0, s>>>(
-          (const bf16*)ybuf, h->dst_row.as<int32_t>(), h->wts.as<float>(), dense_out, shared_out, (int32_t)T, d, k,
-          (bf16*)out);
+          (const bf16*)ybuf, token_major ? nullptr : h->dst_row.as<int32_t>(), h->wts.as<float>(), dense_out,
+          shared_out, (int32_t)T, d, k, (bf16*)out);
     else
       dispatch::combine_kernel<float, float><<<grid, dispatch::kCombineWarps * 32, 0, s>>>(
           (const float*)ybuf, h->dst_row.as<int32_t>(), h->wts.as<float>(), dense_out, shared_out, (int32_t)T, d, k,
@@ -1733,7 +1755,7 @@ void noor_moe_destroy(noor_moe_handle* h) {
                       &h->dw2, &h->dg32, &h->du32, &h->dd32, &h->sw1, &h->sw2, &h->sg32, &h->su32, &h->sd32,
                       &h->x_in, &h->out_buf, &h->idx, &h->wts, &h->lrank, &h->dst_row, &h->blk_hist,
                       &h->blk_base, &h->counts64, &h->counts_glob, &h->seg_start, &h->mtile_start, &h->scores,
-                      &h->xp, &h->h, &h->y, &h->xrecv, &h->ysend, &h->dense_h, &h->dense_out, &h->shared_h,
+                      &h->xp, &h->h, &h->y, &h->ymap, &h->xrecv, &h->ysend, &h->dense_h, &h->dense_out, &h->shared_h,
                       &h->shared_out, &h->grp_row, &h->grp_mtile, &h->grp_widx, &h->cnt_recv, &h->scan_done,
                       &h->util, &h->smebu_m, &h->pre_w, &h->post_w, &h->xn, &h->ffn};
     for (DevBuf* b : bufs) b->release();

@@ -13,7 +13,8 @@
 //   barrier  every rank's rows have landed;
 //   GEMMs    the expert down projection's epilogue stores each output row
 //            straight back into the buffer of the rank that sent the row, at
-//            that rank's own pick-row number (the single-GPU row layout);
+//            the token-major row t*k + slot the sender recorded beside the
+//            row (the single-GPU layout of y);
 //   barrier  every rank's outputs have landed; the combine gathers locally.
 // Nothing waits on the host, so a whole layer step can be recorded in a CUDA
 // graph.  Every wait is bounded; a rank that gives up writes an error code
@@ -40,6 +41,8 @@ constexpr int STATUS_TIMEOUT = 3;       // a barrier gave up waiting
 struct Peers {
   uint8_t* sync[kMaxRanks];   // every rank's sync area, as mapped in this process
   uint8_t* xrecv[kMaxRanks];  // every rank's receive buffer (rows of row_bytes)
+  int32_t* rowmap[kMaxRanks]; // every rank's receive row map: for receive row j, the
+                              // sender's token-major output row t*k + slot
   int32_t G;
   int32_t me;
   int64_t timeout_ns;         // bound of every wait on another rank
@@ -311,6 +314,7 @@ __global__ void __launch_bounds__(kPermuteWarps * 32) permute_peer_kernel(
         if (mine) {
           const int32_t remote = __ldg(dest_base + e) + local - __ldg(seg_start + e);
           dst[i] = P.xrecv[r] + (int64_t)remote * row_bytes;
+          if (lane == 1 && store) P.rowmap[r][remote] = t * k + i;
           any = true;
         }
       }

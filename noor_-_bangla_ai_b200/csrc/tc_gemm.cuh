@@ -84,6 +84,13 @@ struct Params {
   const int32_t* out_rank;
   const int32_t* out_shift;
   void* out_peer[8];
+  // EPI_STORE_BF16: when set, output row of the tile's row r is out_rowmap[r]
+  // (the token-major row t*k + slot of the pick that row holds) instead of
+  // r + shift, so the combine finds each token's k rows side by side.
+  const int32_t* out_rowmap;
+  // EPI_COMBINE_BF16: y is token-major (pick (t, i) at row t*k + i) and
+  // dst_row is not read.
+  int32_t y_token_major;
 };
 
 // Output base and row shift of the tile's group.
@@ -153,6 +160,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
       : "memory");
+}
+
+// Bring a tile into L2 ahead of its TMA load (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
 }
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
@@ -284,6 +299,33 @@ __device__ __forceinline__ void write_chunk64_staged(void* C, int64_t ldc, int r
   __syncwarp();  // the buffer is reused by the next chunk
 }
 
+// write_chunk64_staged with a row map: lane i's row (tile row row0 + i)
+// leaves at output row myrow (-1: not written).  Each 128-byte piece takes
+// its row from the lane that holds it.
+__device__ __forceinline__ void write_chunk64_staged_mapped(void* C, int64_t ldc, int32_t myrow, int col,
+                                                            const uint32_t (&p0)[16], const uint32_t (&p1)[16],
+                                                            uint8_t* stage, int lane) {
+  const int sw = lane & 7;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    *reinterpret_cast<uint4*>(stage + lane * 128 + ((j ^ sw) << 4)) =
+        make_uint4(p0[4 * j], p0[4 * j + 1], p0[4 * j + 2], p0[4 * j + 3]);
+    *reinterpret_cast<uint4*>(stage + lane * 128 + (((j + 4) ^ sw) << 4)) =
+        make_uint4(p1[4 * j], p1[4 * j + 1], p1[4 * j + 2], p1[4 * j + 3]);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int piece = lane + 32 * j;
+    const int r = piece >> 3, part = piece & 7;
+    const int32_t orow = __shfl_sync(0xffffffffu, myrow, r);
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + r * 128 + ((part ^ (r & 7)) << 4));
+    if (orow >= 0)
+      *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(C) + (int64_t)orow * ldc + col + part * 8) = v;
+  }
+  __syncwarp();  // the buffer is reused by the next chunk
+}
+
 template <int EPI>
 __device__ __forceinline__ void store_chunk32(void* C, int64_t ldc, int row, int col, const uint32_t (&v)[32],
                                               const uint32_t (&u)[32]) {
@@ -372,7 +414,7 @@ __device__ __forceinline__ void combine_prepare(const Params& p, int32_t row0, i
     dst[i] = 0;
     wv[i] = 0.f;
     if (valid && i < p.k) {
-      dst[i] = __ldg(p.dst_row + (int64_t)row * p.k + i);
+      dst[i] = p.y_token_major ? row * p.k + i : __ldg(p.dst_row + (int64_t)row * p.k + i);
       wv[i] = __ldg(p.wts + (int64_t)row * p.k + i);
     }
   }
@@ -430,6 +472,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
     constexpr int SPAN = BN / 2;
     if constexpr (EPI == EPI_STORE_BF16) {
       if (stage) {
+        const int32_t myrow = !valid ? -1 : (p.out_rowmap ? __ldg(p.out_rowmap + row) : orow);
 #pragma unroll 1
         for (int c = part * SPAN; c < (part + 1) * SPAN; c += 64) {
           uint32_t g0[32], g1[32];
@@ -439,11 +482,14 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
           uint32_t pk0[16], pk1[16];
           activate_chunk32<EPI>(g0, g0, pk0);
           activate_chunk32<EPI>(g1, g1, pk1);
-          write_chunk64_staged(C, p.ldc, wrow0, wrows, nt * BN + c, pk0, pk1, stage, lane);
+          if (p.out_rowmap) write_chunk64_staged_mapped(C, p.ldc, myrow, nt * BN + c, pk0, pk1, stage, lane);
+          else write_chunk64_staged(C, p.ldc, wrow0, wrows, nt * BN + c, pk0, pk1, stage, lane);
         }
         return;
       }
     }
+    // the plain BF16 store may send rows through the row map (token-major y)
+    const int32_t orow_m = (EPI == EPI_STORE_BF16 && p.out_rowmap && valid) ? __ldg(p.out_rowmap + row) : orow;
 #pragma unroll 1
     for (int c = part * SPAN; c < (part + 1) * SPAN; c += 32) {
       uint32_t g[32];
@@ -455,7 +501,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
         uint32_t pk[16];
         activate_chunk32<EPI>(g, g, pk);
         if (stage) write_chunk32_staged(C, p.ldc, wrow0, wrows, nt * BN + c, pk, stage, lane);
-        else if (valid) write_chunk32_direct(C, p.ldc, orow, nt * BN + c, pk);
+        else if (valid) write_chunk32_direct(C, p.ldc, orow_m, nt * BN + c, pk);
       }
     }
   }
@@ -648,7 +694,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // the leader's accumulator-empty barrier.  Tiles are 256 rows: the group
 // table's tile numbering must use BM2 = 256.
 constexpr int BM2 = 256;
-constexpr int STAGES2 = 5;
+// Operand ring depth requested (build-time; each stage is 32 KB a CTA) and
+// how many k-blocks ahead the producer prefetches its tiles into L2 (0: off).
+#ifndef NOOR_GEMM_STAGES
+#define NOOR_GEMM_STAGES 5
+#endif
+#ifndef NOOR_GEMM_PREFETCH_KB
+#define NOOR_GEMM_PREFETCH_KB 0
+#endif
+constexpr int kMaxStages2 = 8;
+constexpr int kPrefetchKB = NOOR_GEMM_PREFETCH_KB;
+constexpr int kSmemLimit = 227 * 1024;
+constexpr int kStaticSmemMargin = 4096;  // group table, barriers
 
 template <int EPI>
 struct Cfg2 {
@@ -659,7 +716,11 @@ struct Cfg2 {
   // for write_chunk32_staged (less shared memory leaves more L1 for the
   // combine's gathers)
   static constexpr int STAGE_OUT_BYTES = EPI == EPI_STORE_BF16 ? 4096 : 2048;
-  static constexpr int SMEM_BYTES = STAGES2 * STAGE_BYTES + EPI_WARPS * STAGE_OUT_BYTES + 1024;
+  // the requested depth, or as many stages as fit beside the output staging
+  static constexpr int FIT = (kSmemLimit - kStaticSmemMargin - EPI_WARPS * STAGE_OUT_BYTES - 1024) / STAGE_BYTES;
+  static constexpr int STAGES = NOOR_GEMM_STAGES < FIT ? NOOR_GEMM_STAGES : FIT;
+  static_assert(STAGES >= 2 && STAGES <= kMaxStages2, "operand ring depth");
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_WARPS * STAGE_OUT_BYTES + 1024;
   static constexpr uint32_t TMEM_COLS = 512;  // two 256-column accumulators
   static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
                                     ((uint32_t)(256 >> 4) << 24);
@@ -729,14 +790,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
   using C = Cfg2<EPI>;
   constexpr int BN = 256;
+  constexpr int STAGES2 = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smA = smem;
   uint8_t* smB = smem + STAGES2 * C::A_BYTES;
-  uint8_t* smOut = smem + STAGES2 * C::STAGE_BYTES;  // EPI_WARPS x 2 KB
+  uint8_t* smOut = smem + STAGES2 * C::STAGE_BYTES;  // EPI_WARPS x STAGE_OUT_BYTES
 
-  __shared__ __align__(8) uint64_t full_bar[STAGES2];
-  __shared__ __align__(8) uint64_t empty_bar[STAGES2];
+  __shared__ __align__(8) uint64_t full_bar[kMaxStages2];
+  __shared__ __align__(8) uint64_t empty_bar[kMaxStages2];
   __shared__ __align__(8) uint64_t accf_bar[2];
   __shared__ __align__(8) uint64_t acce_bar[2];
   __shared__ __align__(8) uint64_t drain_bar;
@@ -792,8 +854,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         const TileCoord tc = decode_tile(groups, tile, p.n_tiles, BM2);
         const int32_t arow = tc.row0 + 128 * (int32_t)rank;
         const int32_t brow = tc.widx * p.N + tc.nt * BN + 128 * (int32_t)rank;
+        // L2 prefetch cursor kPrefetchKB k-blocks ahead, into the next tile
+        [[maybe_unused]] int32_t next_arow = -1, next_brow = 0;
+        if constexpr (kPrefetchKB > 0) {
+          if (tile + nclusters < total_tiles) {
+            const TileCoord nc = decode_tile(groups, tile + nclusters, p.n_tiles, BM2);
+            next_arow = nc.row0 + 128 * (int32_t)rank;
+            next_brow = nc.widx * p.N + nc.nt * BN + 128 * (int32_t)rank;
+          }
+        }
         bool ok = true;
         for (int kb = 0; kb < num_kb; ++kb) {
+          if constexpr (kPrefetchKB > 0) {
+            const int pkb = kb + kPrefetchKB;
+            if (pkb < num_kb) {
+              tma_prefetch_l2_2d(&tmA, pkb * BK, arow);
+              tma_prefetch_l2_2d(&tmB, pkb * BK, brow);
+            } else if (next_arow >= 0 && pkb - num_kb < num_kb) {
+              tma_prefetch_l2_2d(&tmA, (pkb - num_kb) * BK, next_arow);
+              tma_prefetch_l2_2d(&tmB, (pkb - num_kb) * BK, next_brow);
+            }
+          }
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, &abort_flag, p.err, DEV_TIMEOUT_PRODUCER)) {
             ok = false;
             break;
