@@ -2,7 +2,12 @@
 
   python bench.py [--gpus N] [--steps K] [--warmup W]
                   [--config edge|edge_skewed|pro|max_layer|proxy_tiny] [--impl ours|reference]
-                  [--no-pro] [--no-cpu-baseline] [--no-graph]
+                  [--sublayer] [--no-pro] [--no-cpu-baseline] [--no-graph]
+
+--sublayer times the MoE block's FFN sublayer instead of the bare layer:
+h + post_norm(ParallelFFN(pre_norm(h))) through noor_moe_ffn_sublayer_forward
+(block.rs:87-90; norm weights ones as RMSNorm::new, eps 1e-6, the depth scale
+of block 3), so its cost over the bare layer is the two sandwich norms.
 
 A step is one ParallelFFN forward (router, permute, grouped SwiGLU expert
 GEMMs, dense GeGLU branch, combine) over one batch of seeded synthetic tokens,
@@ -87,9 +92,11 @@ def layer_tokens(cfg, world):
     return cfg.tokens, "weak"
 
 
-def config_dict(cfg, T_rank, world, scaling):
+def config_dict(cfg, T_rank, world, scaling, sublayer=False):
     """The workload; identical in both arms for the same --config and N."""
-    return {"workload": f"{cfg.name} MoE layer (ParallelFFN forward)", "tokens_per_rank": T_rank,
+    what = ("MoE block FFN sublayer (sandwich-normed ParallelFFN + residual)" if sublayer
+            else "MoE layer (ParallelFFN forward)")
+    return {"workload": f"{cfg.name} {what}", "tokens_per_rank": T_rank,
             "global_tokens": T_rank * world, "d_model": cfg.d_model, "n_experts": cfg.n_experts,
             "top_k": cfg.top_k, "expert_ff": cfg.expert_ff, "dense_ff": cfg.dense_ff,
             "dense_act": "gelu_tanh (GeGLU)", "parallelism": f"ep{world}" if world > 1 else "single",
@@ -272,7 +279,11 @@ class Ctx:
         return pkg.api.comm_init_rank(bytes(t.cpu().tolist()), self.world, self.rank, self.local_rank)
 
 
-def measure_layer(ctx, cfg, steps, warmup, use_graph, want_e2e, want_parity, clocks=None):
+SUBLAYER_BLOCK = 3  # depth scale 1/sqrt(block + 1) of the timed sublayer
+SUBLAYER_EPS = 1e-6
+
+
+def measure_layer(ctx, cfg, steps, warmup, use_graph, want_e2e, want_parity, clocks=None, sublayer=False):
     """Times one layer's forward over `steps` steps on every rank; returns the
     numbers for rank 0's line (value, ms/step, launches, per-kernel times, e2e,
     ep_parity)."""
@@ -286,17 +297,21 @@ def measure_layer(ctx, cfg, steps, warmup, use_graph, want_e2e, want_parity, clo
     h = pkg.api.Handle(cfg.d_model, cfg.n_experts, cfg.top_k, cfg.expert_ff, cfg.dense_ff, dtype=cfg.dtype,
                        device=ctx.local_rank, world_size=world, rank=rank, max_tokens=T, comm=comm)
     h.load_weights(w)
+    if sublayer:
+        ones = np.ones(cfg.d_model, np.float32)
+        h.set_sandwich(ones, ones, SUBLAYER_EPS, 1.0 / np.sqrt(np.float32(SUBLAYER_BLOCK + 1)))
+    fwd_dev = h.ffn_sublayer_device if sublayer else h.forward_device
 
     x_host = torch.from_numpy(xb.view(np.int16) if cfg.dtype == W.BF16 else xb).pin_memory()
     x_dev = x_host.to(dev)
     out_dev = torch.empty_like(x_dev)
     counts = torch.empty(cfg.n_experts, dtype=torch.int64, device=dev)
-    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)  # written between steps
     stream = torch.cuda.current_stream(dev)
     sid = stream.cuda_stream
 
     def step():
-        h.forward_device(x_dev.data_ptr(), out_dev.data_ptr(), T, sid, counts_ptr=counts.data_ptr())
+        fwd_dev(x_dev.data_ptr(), out_dev.data_ptr(), T, sid, counts_ptr=counts.data_ptr())
 
     for _ in range(warmup):
         flush.zero_()
@@ -313,12 +328,12 @@ def measure_layer(ctx, cfg, steps, warmup, use_graph, want_e2e, want_parity, clo
         cs = torch.cuda.Stream(dev)
         cs.wait_stream(stream)
         with torch.cuda.stream(cs):
-            h.forward_device(x_dev.data_ptr(), out_dev.data_ptr(), T, cs.cuda_stream, counts_ptr=counts.data_ptr())
+            fwd_dev(x_dev.data_ptr(), out_dev.data_ptr(), T, cs.cuda_stream, counts_ptr=counts.data_ptr())
         torch.cuda.synchronize(dev)
         graph = torch.cuda.CUDAGraph()
         l0 = h.launch_count()
         with torch.cuda.graph(graph, stream=cs):
-            h.forward_device(x_dev.data_ptr(), out_dev.data_ptr(), T, cs.cuda_stream, counts_ptr=counts.data_ptr())
+            fwd_dev(x_dev.data_ptr(), out_dev.data_ptr(), T, cs.cuda_stream, counts_ptr=counts.data_ptr())
         launches_per_step = h.launch_count() - l0
         for _ in range(warmup):
             flush.zero_()
@@ -354,7 +369,7 @@ def measure_layer(ctx, cfg, steps, warmup, use_graph, want_e2e, want_parity, clo
         # around each of its kernels
         prof_steps = min(steps, 200)
         h.profile_begin(prof_steps * 16)
-        for i in range(prof_steps):
+        for _ in range(prof_steps):
             flush.zero_()
             step()
         ctx.barrier()
@@ -363,6 +378,7 @@ def measure_layer(ctx, cfg, steps, warmup, use_graph, want_e2e, want_parity, clo
     (tot_ms,) = ctx.max_over_ranks(tot_ms)
     launches = ctx.sum_over_ranks(launches)
     res = {"T": T, "scaling": scaling, "transport": transport, "value": T * world * steps / (tot_ms / 1e3),
+           "kernel_timing": "eager" if graph is not None else "timed region",
            "ms_per_step": tot_ms / steps, "launches": launches, "prof": prof, "clocks": clock_rec,
            "graph": graph is not None, "weights": w, "x": x}
     rows_local = int(counts.sum().item())
@@ -375,7 +391,11 @@ def measure_layer(ctx, cfg, steps, warmup, use_graph, want_e2e, want_parity, clo
                              device=ctx.local_rank, max_tokens=T)
         ref.load_weights(w)
         ref_out = torch.empty_like(out_dev)
-        ref.forward_device(x_dev.data_ptr(), ref_out.data_ptr(), T, sid)
+        if sublayer:
+            ref.set_sandwich(ones, ones, SUBLAYER_EPS, 1.0 / np.sqrt(np.float32(SUBLAYER_BLOCK + 1)))
+            ref.ffn_sublayer_device(x_dev.data_ptr(), ref_out.data_ptr(), T, sid)
+        else:
+            ref.forward_device(x_dev.data_ptr(), ref_out.data_ptr(), T, sid)
         ref.sync(sid)
         same = bool(torch.equal(ref_out, out_dev))
         ref.close()
@@ -415,8 +435,7 @@ def measure_layer(ctx, cfg, steps, warmup, use_graph, want_e2e, want_parity, clo
         s_up, s_cmp, s_dn = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
         def fwd(b):
-            h.forward_device(x_buf[b].data_ptr(), out_buf[b].data_ptr(), T, s_cmp.cuda_stream,
-                             counts_ptr=counts.data_ptr())
+            fwd_dev(x_buf[b].data_ptr(), out_buf[b].data_ptr(), T, s_cmp.cuda_stream, counts_ptr=counts.data_ptr())
 
         s_cmp.wait_stream(stream)
         pgraphs = None
@@ -536,13 +555,13 @@ def run_ours(args):
 
     sampler = ClockSampler(local_rank)
     r = measure_layer(ctx, cfg, args.steps, args.warmup, not args.no_graph, want_e2e=True,
-                      want_parity=True, clocks=sampler)
+                      want_parity=True, clocks=sampler, sublayer=args.sublayer)
     T = r["T"]
     clocks = r["clocks"]
     kern = kernel_rooflines(cfg, T, r["prof"], pk, clocks.get("sm_mhz"))
 
     pro = None
-    if cfg.name != "pro" and not args.no_pro:
+    if cfg.name != "pro" and not args.no_pro and not args.sublayer:
         try:
             pc = W.CONFIGS["pro"]
             rp = measure_layer(ctx, pc, PRO_STEPS, args.warmup, not args.no_graph, want_e2e=False,
@@ -576,12 +595,12 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
             "scaling": r["scaling"], "vs_baseline": None, "dtype": "bf16" if cfg.dtype == W.BF16 else "f32",
             "data": "synthetic (seeded Philox; x = RMSNorm(N(0,1)), weights N(0,0.02), bias U(-0.1,0.1))",
-            "config": config_dict(cfg, T, world, r["scaling"]),
+            "config": config_dict(cfg, T, world, r["scaling"], args.sublayer),
             "ep_transport": r["transport"],
             "e2e": r["e2e"],
             "gpu_launches": r["launches"],
-            "timing": ("CUDA-graph replay of one forward per step; per-kernel times from an uncaptured pass"
-                       if r["graph"] else "plain calls; per-kernel events in the timed region"),
+            "timing": {"eager": "CUDA-graph replay of one forward per step; per-kernel times from an uncaptured pass",
+                       "timed region": "plain calls; per-kernel events in the timed region"}[r["kernel_timing"]],
             "roofline": roof,
             "kernels": kern,
             "clocks": clocks,
@@ -590,7 +609,7 @@ def run_ours(args):
             line["ep_parity"] = r["ep_parity"]
         if pro is not None:
             line["pro"] = pro
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and not args.sublayer:
             v, cores, dt, n, blas = cpu_baseline(cfg, r["weights"], r["x"])
             line["cpu_baseline"] = {
                 "value": v, "unit": UNIT, "cores": cores, "kind": "port",
@@ -614,6 +633,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pro", action="store_true", help="skip the extra Pro-like pass")
+    ap.add_argument("--sublayer", action="store_true",
+                    help="time the MoE block's FFN sublayer (sandwich norms + residual) instead of the bare layer")
     ap.add_argument("--no-graph", action="store_true", help="time plain calls instead of a captured forward")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":

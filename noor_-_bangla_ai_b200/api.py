@@ -22,7 +22,9 @@ import numpy as np
 from . import workloads as _w
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libnoor_moe.so")
+# NOOR_MOE_CHECK=1 loads the bounds-checked debug build (build.py --check).
+LIB_PATH = os.path.join(_HERE, "libnoor_moe_check.so" if os.environ.get("NOOR_MOE_CHECK") == "1"
+                        else "libnoor_moe.so")
 
 NOOR_MOE_OK = 0
 ERR_NAMES = {1: "INVALID", 2: "CUDA", 3: "NCCL", 4: "OOM", 5: "STATE", 6: "TIMEOUT", 7: "UNSUPPORTED"}

@@ -21,6 +21,22 @@ enum DevError : int {
   DEV_PEER_PLAN = 6,     // the expert-parallel plan was refused (over-capacity batch)
 };
 
+// Bounds checks of the debug build (compiled with -DNOOR_CHECK): a
+// data-dependent index outside its buffer records DEV_BAD_INDEX in the
+// device error word (err, nullable) and the caller skips the access -- no
+// trap, so the context stays usable and the host reports the error.  Without
+// NOOR_CHECK the check is compiled out and always passes.
+__device__ __forceinline__ bool in_bounds(bool ok, int* err) {
+#ifdef NOOR_CHECK
+  if (!ok && err != nullptr) atomicCAS(err, 0, DEV_BAD_INDEX);
+  return ok;
+#else
+  (void)ok;
+  (void)err;
+  return true;
+#endif
+}
+
 // ~2 s at the B200's 1.9 GHz boost clock; no healthy wait comes close.
 constexpr long long kWaitLimitCycles = 4000000000LL;
 

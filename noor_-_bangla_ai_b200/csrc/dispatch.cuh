@@ -111,61 +111,6 @@ __device__ void scan_segments_block(const int32_t* __restrict__ hist, int32_t nb
   finish_segments(E, BM, s_seg, counts, seg_start, mtile_start, util, k);
 }
 
-// The same scan with the histograms staged in shared memory (buf, buf_ints
-// ints): one coalesced read of the histograms and one coalesced write of the
-// bases, instead of strided L2 round trips per thread.  Falls back to
-// scan_segments_block when they do not fit.
-__device__ void scan_segments_block_staged(const int32_t* __restrict__ hist, int32_t nblk, int32_t E, int32_t BM,
-                                           int64_t* __restrict__ counts, int32_t* __restrict__ seg_start,
-                                           int32_t* __restrict__ blk_base, int32_t* __restrict__ mtile_start,
-                                           int32_t* s_warp, int32_t* s_seg, int64_t* __restrict__ util, int32_t k,
-                                           int32_t* buf, int32_t buf_ints) {
-  const int N = E * nblk;
-  if (N > buf_ints) {
-    scan_segments_block(hist, nblk, E, BM, counts, seg_start, blk_base, mtile_start, s_warp, s_seg, util, k);
-    return;
-  }
-  const int nt = blockDim.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = nt >> 5;
-  {
-    constexpr int U = 8;  // eight independent L2 loads in flight per thread
-    for (int base = threadIdx.x; base < N; base += nt * U) {
-      int v[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) v[u] = base + u * nt < N ? __ldcg(hist + base + u * nt) : 0;
-#pragma unroll
-      for (int u = 0; u < U; ++u)
-        if (base + u * nt < N) buf[base + u * nt] = v[u];
-    }
-  }
-  __syncthreads();
-  const int per = (N + nt - 1) / nt;
-  const int i0 = min(N, (int)threadIdx.x * per), i1 = min(N, i0 + per);
-  int sum = 0;
-  for (int i = i0; i < i1; ++i) sum += buf[i];
-  const int incl = warp_inclusive_scan(sum);
-  if (lane == 31) s_warp[warp] = incl;
-  __syncthreads();
-  if (warp == 0) {
-    const int v = lane < nwarps ? s_warp[lane] : 0;
-    const int vi = warp_inclusive_scan(v);
-    if (lane < nwarps) s_warp[lane] = vi - v;
-    if (lane == nwarps - 1) s_seg[E] = vi;  // total picks
-  }
-  __syncthreads();
-  int run = s_warp[warp] + incl - sum;
-  for (int i = i0; i < i1; ++i) {  // in place: histogram -> exclusive bases
-    const int v = buf[i];
-    buf[i] = run;
-    run += v;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < N; i += nt) blk_base[i] = buf[i];
-  for (int e = threadIdx.x; e < E; e += nt) s_seg[e] = buf[e * nblk];
-  __syncthreads();
-  finish_segments(E, BM, s_seg, counts, seg_start, mtile_start, util, k);
-}
-
 // err (nullable): the router's device error word.  When it is set (a
 // bounded wait in the router gave up, so some picks are placeholders), every
 // count is written as -1 instead, so a caller without a handle sees the
@@ -191,7 +136,8 @@ __global__ void __launch_bounds__(kScanThreads) scan_segments_kernel(const int32
 
 // Each warp takes tokens in a grid-stride loop: it reads the token's row once
 // (up to 4 KB in one batch of 16-byte loads) and writes it to the row of each
-// of its k picks, recording that row in dst_row[t, slot] and, when ymap is
+// of its k picks -- seg_start[e] + blk_base[e][block] + lrank, the router's
+// segment tables -- recording that row in dst_row[t, slot] and, when ymap is
 // given, the inverse ymap[row] = t*k + slot (where the expert down
 // projection puts that row's output: token-major, so the combine reads each
 // token's k rows side by side).  Launched either with a block per 4 tokens,
@@ -202,7 +148,8 @@ constexpr int kPermuteWarps = 4;
 __global__ void __launch_bounds__(kPermuteWarps * 32) permute_rows_kernel(
     const uint8_t* __restrict__ x, int32_t row_bytes, int32_t T, int32_t k, int32_t nblk, int32_t tpb,
     const int32_t* __restrict__ idx, const int32_t* __restrict__ lrank, const int32_t* __restrict__ blk_base,
-    uint8_t* __restrict__ xp, int32_t* __restrict__ dst_row, int32_t* __restrict__ ymap) {
+    const int32_t* __restrict__ seg_start, uint8_t* __restrict__ xp, int32_t* __restrict__ dst_row,
+    int32_t* __restrict__ ymap, int64_t rows_cap, int* err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nvec = row_bytes >> 4;
   constexpr int U = 8;
@@ -213,9 +160,10 @@ __global__ void __launch_bounds__(kPermuteWarps * 32) permute_rows_kernel(
     for (int i = 0; i < 8; ++i) {
       if (i < k) {
         const int32_t e = __ldg(idx + (int64_t)t * k + i);
-        dst[i] = __ldg(bb + (int64_t)e * nblk) + __ldg(lrank + (int64_t)t * k + i);
+        dst[i] = __ldg(seg_start + e) + __ldg(bb + (int64_t)e * nblk) + __ldg(lrank + (int64_t)t * k + i);
+        if (!in_bounds(e >= 0 && dst[i] >= 0 && dst[i] < rows_cap, lane == 0 ? err : nullptr)) dst[i] = -1;
         if (lane == 0) dst_row[(int64_t)t * k + i] = dst[i];
-        if (lane == 1 && ymap != nullptr) ymap[dst[i]] = t * k + i;
+        if (lane == 1 && ymap != nullptr && dst[i] >= 0) ymap[dst[i]] = t * k + i;
       }
     }
     const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)t * row_bytes);
@@ -226,7 +174,7 @@ __global__ void __launch_bounds__(kPermuteWarps * 32) permute_rows_kernel(
         if (base + 32 * u < nvec) v[u] = __ldg(src + base + 32 * u);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        if (i < k) {
+        if (i < k && dst[i] >= 0) {
           uint4* d = reinterpret_cast<uint4*>(xp + (int64_t)dst[i] * row_bytes);
 #pragma unroll
           for (int u = 0; u < U; ++u)
@@ -278,7 +226,7 @@ template <typename YT, typename OT>
 __global__ void __launch_bounds__(kCombineWarps * 32) combine_kernel(
     const YT* __restrict__ y, const int32_t* __restrict__ dst_row, const float* __restrict__ wts,
     const float* __restrict__ dense, const float* __restrict__ shared, int32_t T, int32_t d, int32_t k,
-    OT* __restrict__ out) {
+    OT* __restrict__ out, int64_t y_rows, int* err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int32_t t = blockIdx.x * kCombineWarps + warp;
   if (t >= T) return;
@@ -288,6 +236,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32) combine_kernel(
   for (int i = 0; i < 8; ++i)
     if (i < k) {
       rows[i] = dst_row != nullptr ? __ldg(dst_row + (int64_t)t * k + i) : t * k + i;
+      if (!in_bounds(rows[i] >= 0 && rows[i] < y_rows, lane == 0 ? err : nullptr)) rows[i] = -1;
       w[i] = __ldg(wts + (int64_t)t * k + i);
     }
   const float inv_sqrt2 = 0x1.6a09e6p-1f;  // 1.0f32 / 2.0f32.sqrt() = 0.70710677
@@ -295,7 +244,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32) combine_kernel(
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      if (i < k) {
+      if (i < k && rows[i] >= 0) {
         float v[8];
         Vec8<YT>::load(y + (int64_t)rows[i] * d + c, v);
 #pragma unroll

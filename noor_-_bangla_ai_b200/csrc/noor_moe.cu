@@ -66,12 +66,17 @@ static int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+// A failed runtime call is reported by the call that made it; the runtime's
+// last-error state is cleared so that it does not resurface as the launch
+// error of a later, unrelated call (faults that poison the context stay).
 #define CK(call)                                                                                       \
   do {                                                                                                 \
     cudaError_t e_ = (call);                                                                           \
-    if (e_ != cudaSuccess)                                                                             \
+    if (e_ != cudaSuccess) {                                                                           \
+      (void)cudaGetLastError();                                                                        \
       return fail(e_ == cudaErrorMemoryAllocation ? NOOR_MOE_ERR_OOM : NOOR_MOE_ERR_CUDA,              \
                   "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__);                \
+    }                                                                                                  \
   } while (0)
 
 #define CKN(call)                                                                                      \
@@ -213,6 +218,7 @@ struct noor_moe_handle {
   DevBuf x_in, out_buf, idx, wts, lrank, dst_row, blk_hist, blk_base, counts64, counts_glob, seg_start, mtile_start;
   DevBuf scores;
   DevBuf scan_done;  // zeroed counter for the router's fused scan
+  DevBuf seg_acc;    // [E] zeroed running per-expert totals of the router's blocks
   DevBuf xp, h, y, xrecv, ysend;
   DevBuf ymap;  // [picks] token-major output row of each expert-ordered row (BF16, one GPU)
   DevBuf dense_h, dense_out, shared_h, shared_out;
@@ -404,6 +410,9 @@ int check_device_error(noor_moe_handle* h) {
     h->comm_broken = true;
     return fail(NOOR_MOE_ERR_TIMEOUT, "a wait on another rank gave up; the expert-parallel exchange is closed");
   }
+  if (err == noor::DEV_BAD_INDEX)
+    return fail(NOOR_MOE_ERR_INVALID, "a bounds check of the debug build failed: a kernel found a row index "
+                "outside its buffer and skipped the access");
   return fail(NOOR_MOE_ERR_TIMEOUT, "a kernel's bounded wait gave up (device code %d)", err);
 }
 
@@ -500,6 +509,7 @@ struct CombineArgs {
   const float* shared;
   int32_t k;
   bool y_token_major;  // y row of pick (t, i) is t*k + i (dst_row unused)
+  int64_t y_rows;      // rows y holds (bounds checks of the debug build)
 };
 
 // Where the plain-store epilogue puts its rows.  Expert parallelism over
@@ -552,10 +562,12 @@ int ensure_smem_limit(K kern, int bytes) {
   return NOOR_MOE_OK;
 }
 
+// c_rows: rows the output buffer(s) hold, for the bounds checks of the
+// debug build (0: unchecked).
 template <int BN, int EPI>
 int launch_tc(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& tA, const CUtensorMap& tB,
               const GroupTable& gt, int N, int K, void* C, int64_t ldc, int64_t max_mtiles,
-              const CombineArgs* comb = nullptr, const PeerOut* po = nullptr) {
+              const CombineArgs* comb = nullptr, const PeerOut* po = nullptr, int64_t c_rows = 0) {
   using Cf = tc::Cfg<BN>;
   auto kern = tc::grouped_gemm_kernel<BN, EPI>;
   CKR(ensure_smem_limit(kern, Cf::SMEM_BYTES));
@@ -567,6 +579,7 @@ int launch_tc(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& t
   p.C = C;
   p.ldc = ldc;
   p.err = h->d_err;
+  p.out_rows = c_rows;
   if (comb) {
     p.y = static_cast<const bf16*>(comb->y);
     p.dst_row = comb->dst_row;
@@ -574,6 +587,7 @@ int launch_tc(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& t
     p.shared = comb->shared;
     p.k = comb->k;
     p.y_token_major = comb->y_token_major ? 1 : 0;
+    p.y_rows = comb->y_rows;
   }
   set_peer_out(p, po);
   const int64_t tiles = std::max<int64_t>(1, max_mtiles * p.n_tiles);
@@ -584,7 +598,7 @@ int launch_tc(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& t
 template <int EPI>
 int launch_tc2(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& tA, const CUtensorMap& tB,
                const GroupTable& gt, int N, int K, void* C, int64_t ldc, int64_t max_tiles,
-               const CombineArgs* comb = nullptr, const PeerOut* po = nullptr) {
+               const CombineArgs* comb = nullptr, const PeerOut* po = nullptr, int64_t c_rows = 0) {
   auto kern = tc::grouped_gemm_2cta_kernel<EPI>;
   CKR(ensure_smem_limit(kern, tc::Cfg2<EPI>::SMEM_BYTES));
   tc::Params p{};
@@ -595,6 +609,7 @@ int launch_tc2(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& 
   p.C = C;
   p.ldc = ldc;
   p.err = h->d_err;
+  p.out_rows = c_rows;
   if (comb) {
     p.y = static_cast<const bf16*>(comb->y);
     p.dst_row = comb->dst_row;
@@ -602,6 +617,7 @@ int launch_tc2(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& 
     p.shared = comb->shared;
     p.k = comb->k;
     p.y_token_major = comb->y_token_major ? 1 : 0;
+    p.y_rows = comb->y_rows;
   }
   set_peer_out(p, po);
   const int64_t tiles = std::max<int64_t>(1, max_tiles * p.n_tiles);
@@ -616,13 +632,13 @@ int launch_tc2(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& 
 template <int EPI>
 int launch_gemm(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& tA, const CUtensorMap& tB,
                 const GroupTable& gt, int N, int K, void* C, int64_t ldc, int64_t max_tiles,
-                const CombineArgs* comb = nullptr, const PeerOut* po = nullptr) {
-  if (h->pair2) return launch_tc2<EPI>(h, s, kind, tA, tB, gt, N, K, C, ldc, max_tiles, comb, po);
-  if (N % 256 == 0) return launch_tc<256, EPI>(h, s, kind, tA, tB, gt, N, K, C, ldc, max_tiles, comb, po);
+                const CombineArgs* comb = nullptr, const PeerOut* po = nullptr, int64_t c_rows = 0) {
+  if (h->pair2) return launch_tc2<EPI>(h, s, kind, tA, tB, gt, N, K, C, ldc, max_tiles, comb, po, c_rows);
+  if (N % 256 == 0) return launch_tc<256, EPI>(h, s, kind, tA, tB, gt, N, K, C, ldc, max_tiles, comb, po, c_rows);
   if constexpr (tc::epi_gated(EPI)) {
     return fail(NOOR_MOE_ERR_UNSUPPORTED, "gated GEMM needs N a multiple of 256");
   } else {
-    return launch_tc<128, EPI>(h, s, kind, tA, tB, gt, N, K, C, ldc, max_tiles, comb, po);
+    return launch_tc<128, EPI>(h, s, kind, tA, tB, gt, N, K, C, ldc, max_tiles, comb, po, c_rows);
   }
 }
 
@@ -677,8 +693,10 @@ int glu_up(noor_moe_handle* h, cudaStream_t s, const GluFfn& f) {
   if (h->bf16) {
     const int64_t mt = (f.rows + h->tile_m - 1) / h->tile_m;
     if (f.silu)
-      return launch_gemm<tc::EPI_SWIGLU_BF16>(h, s, f.kind1, *f.tA, *f.tW1, gt, 2 * f.ffn, d, f.hbuf, f.ffn, mt);
-    return launch_gemm<tc::EPI_GEGLU_BF16>(h, s, f.kind1, *f.tA, *f.tW1, gt, 2 * f.ffn, d, f.hbuf, f.ffn, mt);
+      return launch_gemm<tc::EPI_SWIGLU_BF16>(h, s, f.kind1, *f.tA, *f.tW1, gt, 2 * f.ffn, d, f.hbuf, f.ffn, mt,
+                                              nullptr, nullptr, h->capT);
+    return launch_gemm<tc::EPI_GEGLU_BF16>(h, s, f.kind1, *f.tA, *f.tW1, gt, 2 * f.ffn, d, f.hbuf, f.ffn, mt, nullptr,
+                                           nullptr, h->capT);
   }
   const int64_t mt = (f.rows + simt::BM - 1) / simt::BM;
   if (f.silu)
@@ -693,8 +711,11 @@ int glu_down(noor_moe_handle* h, cudaStream_t s, const GluFfn& f, void* out, con
   const int d = h->d;
   if (h->bf16) {
     const int64_t mt = (f.rows + h->tile_m - 1) / h->tile_m;
-    if (comb) return launch_gemm<tc::EPI_COMBINE_BF16>(h, s, f.kind2, *f.tH, *f.tW2, gt, d, f.ffn, out, d, mt, comb);
-    return launch_gemm<tc::EPI_STORE_F32>(h, s, f.kind2, *f.tH, *f.tW2, gt, d, f.ffn, out, d, mt);
+    if (comb)
+      return launch_gemm<tc::EPI_COMBINE_BF16>(h, s, f.kind2, *f.tH, *f.tW2, gt, d, f.ffn, out, d, mt, comb, nullptr,
+                                               f.rows);
+    return launch_gemm<tc::EPI_STORE_F32>(h, s, f.kind2, *f.tH, *f.tW2, gt, d, f.ffn, out, d, mt, nullptr, nullptr,
+                                          h->capT);
   }
   const int64_t mt = (f.rows + simt::BM - 1) / simt::BM;
   return launch_simt<simt::EPI_STORE>(h, s, f.kind2, gt, (const float*)f.hbuf, f.ffn, f.d32, nullptr, 0, d, f.ffn,
@@ -710,6 +731,9 @@ int launch_route_tc(noor_moe_handle* h, cudaStream_t s, const CUtensorMap& tmx, 
                     const router::FusedScan& fs, int* err) {
   const int npad = router::tc_npad(E);
   const int smem = router::tc_smem_bytes(npad);
+  // the epilogue stages the tile's scores in the stage ring
+  if (router::tc_stages(npad) * router::tc_stage_bytes(npad) < router::kTcTPB * (npad + 1) * 4)
+    return fail(NOOR_MOE_ERR_UNSUPPORTED, "router stage ring too small for %d experts", E);
   const unsigned grid = (unsigned)((T + router::kTcTPB - 1) / router::kTcTPB);
   auto go = [&](auto kern) -> int {
     CKR(ensure_smem_limit(kern, smem));
@@ -739,7 +763,7 @@ int run_router(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtensor
   int tpb = 0;
   router::FusedScan fs{h->scan_done.as<int>(), h->counts64.as<int64_t>(), h->seg_start.as<int32_t>(),
                        h->blk_base.as<int32_t>(), h->mtile_start.as<int32_t>(), h->tile_m,
-                       record ? h->util.as<int64_t>() : nullptr};
+                       record ? h->util.as<int64_t>() : nullptr, h->seg_acc.as<int32_t>(), h->d_err};
   if (h->bf16) {
     tpb = router::kTcTPB;
     CKR(launch_route_tc(h, s, *tmx, h->tm_gate, h->bias.as<float>(), h->scales.as<float>(), T, d, E, k, ro, fs,
@@ -1108,7 +1132,8 @@ int run_forward_peer(noor_moe_handle* h, cudaStream_t s, const void* x, const CU
       P::permute_peer_kernel<<<grid, P::kPermuteWarps * 32, 0, st>>>(
           static_cast<const uint8_t*>(x), d * 2, (int32_t)T, k, (int32_t)((T + tpb - 1) / tpb), tpb,
           h->idx.as<int32_t>(), h->lrank.as<int32_t>(), h->blk_base.as<int32_t>(), h->seg_start.as<int32_t>(),
-          h->dest_base.as<int32_t>(), h->El, h->peers, h->pstatus.as<int>(), h->dst_row.as<int32_t>(), part);
+          h->dest_base.as<int32_t>(), h->El, h->peers, h->pstatus.as<int>(), h->dst_row.as<int32_t>(), part,
+          cap_rows, h->d_err);
     });
   };
   const bool split = kSplitPermutePeer && !fork && T > 0;
@@ -1140,21 +1165,22 @@ int run_forward_peer(noor_moe_handle* h, cudaStream_t s, const void* x, const CU
   const int64_t max_mtiles = (cap_rows + h->tile_m - 1) / h->tile_m + E;
   const PeerOut pout{h->grp_orank.as<int32_t>(), h->grp_oshift.as<int32_t>(), h->peer_y, h->prowmap.as<int32_t>()};
   CKR(launch_gemm<tc::EPI_SWIGLU_BF16>(h, s, K_EXPERT_GEMM1, h->tm_pxrecv, h->tm_w1, gt, 2 * h->ff, d, h->h.p, h->ff,
-                                       max_mtiles));
+                                       max_mtiles, nullptr, nullptr, h->cap_recv));
   CKR(launch_gemm<tc::EPI_STORE_BF16>(h, s, K_EXPERT_GEMM2, h->tm_h, h->tm_w2, gt, d, h->ff, nullptr, d, max_mtiles,
-                                      nullptr, &pout));
+                                      nullptr, &pout, h->capP * k));
   CKR(barrier());
   if (T == 0) return NOOR_MOE_OK;
   if (fork) CK(cudaStreamWaitEvent(s, h->ev_join, 0));
   const float* shared_out = h->has_shared ? h->shared_out.as<float>() : nullptr;
   if (h->has_dense) {
-    const CombineArgs comb{h->py.p, h->dst_row.as<int32_t>(), h->wts.as<float>(), shared_out, k, true};
+    const CombineArgs comb{h->py.p, h->dst_row.as<int32_t>(), h->wts.as<float>(), shared_out, k, true, h->capP * k};
     return glu_down(h, s, dense, out, &comb);
   }
   return launch(h, s, K_COMBINE, [&] {
     const unsigned grid = (unsigned)((T + dispatch::kCombineWarps - 1) / dispatch::kCombineWarps);
     dispatch::combine_kernel<bf16, bf16><<<grid, dispatch::kCombineWarps * 32, 0, s>>>(
-        h->py.as<bf16>(), nullptr, h->wts.as<float>(), nullptr, shared_out, (int32_t)T, d, k, (bf16*)out);
+        h->py.as<bf16>(), nullptr, h->wts.as<float>(), nullptr, shared_out, (int32_t)T, d, k, (bf16*)out,
+        h->capP * k, h->d_err);
   });
 }
 
@@ -1224,8 +1250,9 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
       const unsigned grid = (unsigned)(side ? std::min<int64_t>(blocks, h->num_sms) : blocks);
       dispatch::permute_rows_kernel<<<grid, dispatch::kPermuteWarps * 32, 0, s>>>(
           static_cast<const uint8_t*>(x), (int32_t)(d * b), (int32_t)T, k, (int32_t)((T + tpb - 1) / tpb), tpb,
-          h->idx.as<int32_t>(), h->lrank.as<int32_t>(), h->blk_base.as<int32_t>(), h->xp.as<uint8_t>(),
-          h->dst_row.as<int32_t>(), token_major ? h->ymap.as<int32_t>() : nullptr);
+          h->idx.as<int32_t>(), h->lrank.as<int32_t>(), h->blk_base.as<int32_t>(), h->seg_start.as<int32_t>(),
+          h->xp.as<uint8_t>(), h->dst_row.as<int32_t>(), token_major ? h->ymap.as<int32_t>() : nullptr,
+          h->capT * k, h->d_err);
     }));
   }
 
@@ -1265,10 +1292,10 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
   if (max_mtiles > 0) {
     if (h->bf16) {
       CKR(launch_gemm<tc::EPI_SWIGLU_BF16>(h, s, K_EXPERT_GEMM1, *tA, h->tm_w1, gt, 2 * h->ff, d, h->h.p, h->ff,
-                                           max_mtiles));
+                                           max_mtiles, nullptr, nullptr, h->cap_recv));
       const PeerOut ytm{nullptr, nullptr, nullptr, h->ymap.as<int32_t>()};
       CKR(launch_gemm<tc::EPI_STORE_BF16>(h, s, K_EXPERT_GEMM2, h->tm_h, h->tm_w2, gt, d, h->ff, h->y.p, d,
-                                          max_mtiles, nullptr, token_major ? &ytm : nullptr));
+                                          max_mtiles, nullptr, token_major ? &ytm : nullptr, h->cap_recv));
     } else {
       const int64_t ffd = (int64_t)d * h->ff;
       CKR((launch_simt<simt::EPI_SWIGLU>(h, s, K_EXPERT_GEMM1, gt, (const float*)A32, d, h->wg32.as<float>(),
@@ -1284,20 +1311,22 @@ int run_forward(noor_moe_handle* h, cudaStream_t s, const void* x, const CUtenso
   if (T == 0) return NOOR_MOE_OK;
   const float* shared_out = h->has_shared ? h->shared_out.as<float>() : nullptr;
   if (fuse_combine) {
-    const CombineArgs comb{ybuf, h->dst_row.as<int32_t>(), h->wts.as<float>(), shared_out, k, token_major};
+    const int64_t y_rows = h->G > 1 ? h->capT * k : h->cap_recv;  // ysend (NCCL) or y
+    const CombineArgs comb{ybuf, h->dst_row.as<int32_t>(), h->wts.as<float>(), shared_out, k, token_major, y_rows};
     return glu_down(h, s, dense, out, &comb);
   }
   return launch(h, s, K_COMBINE, [&] {
     const unsigned grid = (unsigned)((T + dispatch::kCombineWarps - 1) / dispatch::kCombineWarps);
     const float* dense_out = h->has_dense ? h->dense_out.as<float>() : nullptr;
+    const int64_t y_rows = h->G > 1 ? h->capT * k : h->cap_recv;  // ysend (NCCL) or y
     if (h->bf16)
       dispatch::combine_kernel<bf16, bf16><<<grid, dispatch::kCombineWarps * 32, 0, s>>>(
           (const bf16*)ybuf, token_major ? nullptr : h->dst_row.as<int32_t>(), h->wts.as<float>(), dense_out,
-          shared_out, (int32_t)T, d, k, (bf16*)out);
+          shared_out, (int32_t)T, d, k, (bf16*)out, y_rows, h->d_err);
     else
       dispatch::combine_kernel<float, float><<<grid, dispatch::kCombineWarps * 32, 0, s>>>(
           (const float*)ybuf, h->dst_row.as<int32_t>(), h->wts.as<float>(), dense_out, shared_out, (int32_t)T, d, k,
-          (float*)out);
+          (float*)out, y_rows, h->d_err);
   });
 }
 
@@ -1395,7 +1424,8 @@ int noor_moe_create(const noor_moe_desc* desc, void* nccl_comm, noor_moe_handle*
         cudaMallocHost(&h->h_grp, 3 * (ng + 1) * 4) != cudaSuccess)
       return bail(fail(NOOR_MOE_ERR_OOM, "pinned host buffers"));
   }
-  if (h->scan_done.ensure(sizeof(int)) != NOOR_MOE_OK || cudaMemset(h->scan_done.p, 0, sizeof(int)) != cudaSuccess)
+  if (h->scan_done.ensure(sizeof(int)) != NOOR_MOE_OK || cudaMemset(h->scan_done.p, 0, sizeof(int)) != cudaSuccess ||
+      h->seg_acc.ensure(h->E * 4) != NOOR_MOE_OK || cudaMemset(h->seg_acc.p, 0, h->E * 4) != cudaSuccess)
     return bail(fail(NOOR_MOE_ERR_CUDA, "scan counter setup failed"));
   if (h->util.ensure((h->E + 1) * 8) != NOOR_MOE_OK || cudaMemset(h->util.p, 0, (h->E + 1) * 8) != cudaSuccess ||
       h->smebu_m.ensure(h->E * 4) != NOOR_MOE_OK || cudaMemset(h->smebu_m.p, 0, h->E * 4) != cudaSuccess)
@@ -1529,20 +1559,35 @@ static int launch_norm(noor_moe_handle* h, cudaStream_t s, int kind, const void*
                        const void* resid, int64_t T, void* out) {
   if (T == 0) return NOOR_MOE_OK;
   const unsigned grid = (unsigned)((T + norm::kWarps - 1) / norm::kWarps);
+  const int nv = h->bf16 && h->d % 256 == 0 ? h->d / 256 : 0;  // 16-byte pieces a lane keeps in registers
   return launch(h, s, kind, [&] {
     if (h->bf16) {
-      if (resid)
-        norm::rms_norm_rows_kernel<bf16, true><<<grid, norm::kWarps * 32, 0, s>>>(
-            (const bf16*)x, w, h->norm_eps, h->depth_scale, (const bf16*)resid, (int32_t)T, h->d, (bf16*)out);
-      else
-        norm::rms_norm_rows_kernel<bf16, false><<<grid, norm::kWarps * 32, 0, s>>>(
-            (const bf16*)x, w, h->norm_eps, h->depth_scale, nullptr, (int32_t)T, h->d, (bf16*)out);
+      const bf16* xb = (const bf16*)x;
+      const bf16* rb = (const bf16*)resid;
+      bf16* ob = (bf16*)out;
+#define NOOR_NORM_BF16(NV)                                                                                      \
+  if (resid)                                                                                                   \
+    norm::rms_norm_rows_kernel<bf16, true, NV><<<grid, norm::kWarps * 32, 0, s>>>(xb, w, h->norm_eps,          \
+                                                                                  h->depth_scale, rb,          \
+                                                                                  (int32_t)T, h->d, ob);       \
+  else                                                                                                         \
+    norm::rms_norm_rows_kernel<bf16, false, NV><<<grid, norm::kWarps * 32, 0, s>>>(xb, w, h->norm_eps,         \
+                                                                                   h->depth_scale, nullptr,    \
+                                                                                   (int32_t)T, h->d, ob);
+      switch (nv) {
+        case 4: NOOR_NORM_BF16(4) break;
+        case 8: NOOR_NORM_BF16(8) break;
+        case 12: NOOR_NORM_BF16(12) break;
+        case 16: NOOR_NORM_BF16(16) break;
+        default: NOOR_NORM_BF16(0) break;
+      }
+#undef NOOR_NORM_BF16
     } else {
       if (resid)
-        norm::rms_norm_rows_kernel<float, true><<<grid, norm::kWarps * 32, 0, s>>>(
+        norm::rms_norm_rows_kernel<float, true, 0><<<grid, norm::kWarps * 32, 0, s>>>(
             (const float*)x, w, h->norm_eps, h->depth_scale, (const float*)resid, (int32_t)T, h->d, (float*)out);
       else
-        norm::rms_norm_rows_kernel<float, false><<<grid, norm::kWarps * 32, 0, s>>>(
+        norm::rms_norm_rows_kernel<float, false, 0><<<grid, norm::kWarps * 32, 0, s>>>(
             (const float*)x, w, h->norm_eps, h->depth_scale, nullptr, (int32_t)T, h->d, (float*)out);
     }
   });
@@ -1757,6 +1802,7 @@ void noor_moe_destroy(noor_moe_handle* h) {
                       &h->blk_base, &h->counts64, &h->counts_glob, &h->seg_start, &h->mtile_start, &h->scores,
                       &h->xp, &h->h, &h->y, &h->ymap, &h->xrecv, &h->ysend, &h->dense_h, &h->dense_out, &h->shared_h,
                       &h->shared_out, &h->grp_row, &h->grp_mtile, &h->grp_widx, &h->cnt_recv, &h->scan_done,
+                      &h->seg_acc,
                       &h->util, &h->smebu_m, &h->pre_w, &h->post_w, &h->xn, &h->ffn};
     for (DevBuf* b : bufs) b->release();
     if (h->h_cnt) cudaFreeHost(h->h_cnt);
@@ -2020,7 +2066,7 @@ extern "C" int noor_moe_route_static(const void* x, const void* gate, const floa
   CK(cudaMemsetAsync(err, 0, sizeof(int), s));
   router::RouterOut ro{idx, w, reinterpret_cast<int32_t*>(sb + off_lrank), reinterpret_cast<int32_t*>(sb + off_hist)};
   float* scores = reinterpret_cast<float*>(sb + off_scores);
-  const router::FusedScan nofs{nullptr, nullptr, nullptr, nullptr, nullptr, tc::BM, nullptr};
+  const router::FusedScan nofs{nullptr, nullptr, nullptr, nullptr, nullptr, tc::BM, nullptr, nullptr, nullptr};
   if (dtype == NOOR_DTYPE_BF16) {
     // the same kernel as noor_moe_route, so the results are identical; the
     // tensor maps are encoded on the host for this call (no allocation)

@@ -8,11 +8,10 @@
 // the RMS in f64, the result rounded to f32; Tensor::scale and tensor::add
 // (tensor.rs:222-229, 280-288) are plain f32 multiplies and adds.
 //
-// One warp per row.  The row is read twice (the second read hits L1/L2):
-// once for the sum of squares, once to normalise.  Each lane sums its
-// elements in f64 in order and the lanes are combined by a fixed butterfly,
-// so the result is deterministic; its association differs from the
-// reference's single running sum only in the last bits of an f64.
+// One warp per row.  Each lane sums its elements in f64 in order and the
+// lanes are combined by a fixed butterfly, so the result is deterministic;
+// its association differs from the reference's single running sum only in
+// the last bits of an f64.
 #pragma once
 
 #include "common.cuh"
@@ -49,9 +48,31 @@ struct Row8<float> {
   }
 };
 
-// out[t] = (resid[t] +) f32(f64(x[t]) / rms * f64(w)) * depth_scale.
-// d must be a multiple of 8 and rows 16-byte aligned.
-template <typename T_, bool RESID>
+// x / rms in f64, correctly rounded, without a divide per element:
+// Markstein's correction (P. Markstein, "Computation of elementary functions
+// on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990): with
+// r = RN(1/rms), q = RN(x r) and the exact residual e = x - q rms (one FMA),
+// RN(q + e r) = RN(x / rms) for operands away from overflow and underflow,
+// which holds here (rms >= sqrt(eps) > 0, x finite).
+__device__ __forceinline__ double div_by_rms(double x, double rms, double r) {
+  const double q = __dmul_rn(x, r);
+  const double e = __fma_rn(-q, rms, x);
+  return __fma_rn(e, r, q);
+}
+
+// One element of the output: f32(x / rms * w) * depth_scale (+ resid).
+__device__ __forceinline__ float norm_one(float x, double rms, double r, float w, float depth_scale) {
+  return __fmul_rn(__double2float_rn(__dmul_rn(div_by_rms((double)x, rms, r), (double)w)), depth_scale);
+}
+
+// out[t] = (resid[t] +) f32(f64(x[t]) / rms * f64(w)) * depth_scale, rms =
+// sqrt(sum_i x_i^2 / d + eps) in f64 (x_i^2 is exact in f64, so a fused
+// multiply-add equals the reference's multiply then add).
+// NV > 0 (BF16 rows, d = 256 * NV): each lane keeps its NV 16-byte pieces of
+// the row in registers, so the row is read from memory once.  NV == 0: any d
+// that is a multiple of 8, the row read twice (the second time from L1/L2).
+// Rows 16-byte aligned.
+template <typename T_, bool RESID, int NV>
 __global__ void __launch_bounds__(kWarps * 32) rms_norm_rows_kernel(const T_* __restrict__ x,
                                                                     const float* __restrict__ w, double eps,
                                                                     float depth_scale, const T_* __restrict__ resid,
@@ -61,31 +82,74 @@ __global__ void __launch_bounds__(kWarps * 32) rms_norm_rows_kernel(const T_* __
   if (t >= T) return;
   const T_* row = x + (int64_t)t * d;
   double ss = 0.0;
-  for (int c = lane * 8; c < d; c += 256) {
-    float v[8];
-    Row8<T_>::load(row + c, v);
+  if constexpr (NV > 0) {
+    static_assert(sizeof(T_) == 2, "register-resident rows are BF16");
+    uint4 v[NV];
+    const uint4* rv = reinterpret_cast<const uint4*>(row);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) ss = __dadd_rn(ss, __dmul_rn((double)v[j], (double)v[j]));
-  }
+    for (int i = 0; i < NV; ++i) v[i] = __ldg(rv + lane + 32 * i);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-  const double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)d), eps));
-  for (int c = lane * 8; c < d; c += 256) {
-    float v[8], o[8];
-    Row8<T_>::load(row + c, v);
-    const float4 wa = __ldg(reinterpret_cast<const float4*>(w + c));
-    const float4 wb = __ldg(reinterpret_cast<const float4*>(w + c + 4));
-    const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+    for (int i = 0; i < NV; ++i) {
+      const uint32_t u[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      o[j] = __fmul_rn(__double2float_rn(__dmul_rn(__ddiv_rn((double)v[j], rms), (double)wv[j])), depth_scale);
-    if constexpr (RESID) {
-      float r[8];
-      Row8<T_>::load(resid + (int64_t)t * d + c, r);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = __fadd_rn(r[j], o[j]);
+      for (int j = 0; j < 4; ++j) {
+        const double a = (double)bf16_lo(u[j]), b = (double)bf16_hi(u[j]);
+        ss = __fma_rn(a, a, ss);
+        ss = __fma_rn(b, b, ss);
+      }
     }
-    Row8<T_>::store(out + (int64_t)t * d + c, o);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    const double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)d), eps));
+    const double r = __drcp_rn(rms);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (lane + 32 * i) * 8;
+      const float4 wa = __ldg(reinterpret_cast<const float4*>(w + c));
+      const float4 wb = __ldg(reinterpret_cast<const float4*>(w + c + 4));
+      const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+      const uint32_t u[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        o[2 * j] = norm_one(bf16_lo(u[j]), rms, r, wv[2 * j], depth_scale);
+        o[2 * j + 1] = norm_one(bf16_hi(u[j]), rms, r, wv[2 * j + 1], depth_scale);
+      }
+      if constexpr (RESID) {
+        float rr[8];
+        Row8<T_>::load(resid + (int64_t)t * d + c, rr);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = __fadd_rn(rr[j], o[j]);
+      }
+      Row8<T_>::store(out + (int64_t)t * d + c, o);
+    }
+  } else {
+    for (int c = lane * 8; c < d; c += 256) {
+      float v[8];
+      Row8<T_>::load(row + c, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = __fma_rn((double)v[j], (double)v[j], ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    const double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)d), eps));
+    const double r = __drcp_rn(rms);
+    for (int c = lane * 8; c < d; c += 256) {
+      float v[8], o[8];
+      Row8<T_>::load(row + c, v);
+      const float4 wa = __ldg(reinterpret_cast<const float4*>(w + c));
+      const float4 wb = __ldg(reinterpret_cast<const float4*>(w + c + 4));
+      const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = norm_one(v[j], rms, r, wv[j], depth_scale);
+      if constexpr (RESID) {
+        float rr[8];
+        Row8<T_>::load(resid + (int64_t)t * d + c, rr);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = __fadd_rn(rr[j], o[j]);
+      }
+      Row8<T_>::store(out + (int64_t)t * d + c, o);
+    }
   }
 }
 

@@ -293,7 +293,7 @@ __global__ void __launch_bounds__(kPermuteWarps * 32) permute_peer_kernel(
     const uint8_t* __restrict__ x, int32_t row_bytes, int32_t T, int32_t k, int32_t nblk, int32_t tpb,
     const int32_t* __restrict__ idx, const int32_t* __restrict__ lrank, const int32_t* __restrict__ blk_base,
     const int32_t* __restrict__ seg_start, const int32_t* __restrict__ dest_base, int32_t El, Peers P,
-    const int* __restrict__ status, int32_t* __restrict__ dst_row, int32_t part) {
+    const int* __restrict__ status, int32_t* __restrict__ dst_row, int32_t part, int64_t cap_rows, int* err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool store = *status == STATUS_OK;
   const int nvec = row_bytes >> 4;
@@ -307,15 +307,18 @@ __global__ void __launch_bounds__(kPermuteWarps * 32) permute_peer_kernel(
       dst[i] = nullptr;
       if (i < k) {
         const int32_t e = __ldg(idx + (int64_t)t * k + i);
-        const int32_t local = __ldg(bb + (int64_t)e * nblk) + __ldg(lrank + (int64_t)t * k + i);
+        const int32_t in_seg = __ldg(bb + (int64_t)e * nblk) + __ldg(lrank + (int64_t)t * k + i);
+        const int32_t local = __ldg(seg_start + e) + in_seg;
         if (lane == 0 && part != PERMUTE_REMOTE) dst_row[(int64_t)t * k + i] = local;
         const int32_t r = e / El;
         const bool mine = part == PERMUTE_ALL || ((r == P.me) == (part == PERMUTE_LOCAL));
         if (mine) {
-          const int32_t remote = __ldg(dest_base + e) + local - __ldg(seg_start + e);
-          dst[i] = P.xrecv[r] + (int64_t)remote * row_bytes;
-          if (lane == 1 && store) P.rowmap[r][remote] = t * k + i;
-          any = true;
+          const int32_t remote = __ldg(dest_base + e) + in_seg;
+          if (in_bounds(r >= 0 && r < P.G && remote >= 0 && remote < cap_rows, lane == 0 ? err : nullptr)) {
+            dst[i] = P.xrecv[r] + (int64_t)remote * row_bytes;
+            if (lane == 1 && store) P.rowmap[r][remote] = t * k + i;
+            any = true;
+          }
         }
       }
     }

@@ -31,12 +31,22 @@ constexpr int kMaxExpertsTC = 128;  // BF16 router: N = roundup(E, 16) <= 128 TM
 
 // sel[slot * TPB + tok] holds the expert of each pick in the block (-1 for
 // tokens past T).  Computes each pick's rank among the block's picks of the
-// same expert in (slot, token) order, writes it to lrank_out[token*k + slot],
-// and writes the block histogram hist_out[e * hist_stride].
+// same expert in (slot, token) order and writes it to lrank_out[token*k +
+// slot].  Then, per expert e with picks in the block, either
+//   seg_acc == nullptr: the block histogram hist_out[e * hist_stride], for a
+//                       later scan over all blocks (dispatch::scan_segments_*);
+//   seg_acc != nullptr: the block claims its rows of expert e's segment with
+//                       one atomicAdd on the running total seg_acc[e] and
+//                       writes the first of them, relative to the segment
+//                       start, to hist_out[e * hist_stride].
+// The claim order between blocks varies from call to call, so the order of
+// rows inside a segment does too; every row is computed on its own by the
+// GEMMs and returns to its token through the row map, so the outputs do not
+// depend on it.
 __device__ void rank_block_picks(const int32_t* sel, int k, int TPB, int E, int T, int32_t tok_base,
                                  int32_t* chunk_cnt /* smem [nchunks][E] */,
                                  int32_t* intra /* smem [k*TPB] */, int32_t* lrank_out,
-                                 int32_t* hist_out, int32_t hist_stride) {
+                                 int32_t* hist_out, int32_t hist_stride, int32_t* seg_acc = nullptr) {
   const int nchunks = (k * TPB + 31) / 32;  // sel is padded with -1 to whole warps
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   for (int i = threadIdx.x; i < nchunks * E; i += blockDim.x) chunk_cnt[i] = 0;
@@ -57,7 +67,8 @@ __device__ void rank_block_picks(const int32_t* sel, int k, int TPB, int E, int 
       chunk_cnt[c * E + e] = run;
       run += v;
     }
-    hist_out[(int64_t)e * hist_stride] = run;
+    if (seg_acc == nullptr) hist_out[(int64_t)e * hist_stride] = run;
+    else if (run > 0) hist_out[(int64_t)e * hist_stride] = atomicAdd(seg_acc + e, run);
   }
   __syncthreads();
   for (int a = threadIdx.x; a < k * TPB; a += blockDim.x) {
@@ -78,18 +89,47 @@ struct RouterOut {
   int32_t* blk_hist; // [E, nblk], expert-major
 };
 
-// Optional scan fused into the router: the last block to finish turns the
-// block histograms into the segment tables (dispatch::scan_segments_block).
-// `done` is a zero-initialised counter the last block resets to zero.
+// Segment tables built inside the router.  Every block claims its rows of
+// each expert's segment from the running totals seg_acc (rank_block_picks),
+// writing blk_base[e][block] relative to the segment start; the last block to
+// finish turns the totals into the counts, the segment starts, the GEMM tile
+// table and the utilization (finish_from_totals), and resets `done` and
+// seg_acc to zero for the next call.
 struct FusedScan {
-  int* done;               // nullptr: no fused scan
+  int* done;               // nullptr: no fused tables (the router writes block histograms)
   int64_t* counts;
   int32_t* seg_start;
-  int32_t* blk_base;
+  int32_t* blk_base;       // [E][nblk] first row of block b's picks of e, relative to seg_start[e]
   int32_t* mtile_start;
   int32_t BM;
-  int64_t* util;           // nullable: utilization accumulator [E+1] (dispatch::scan_segments_block)
+  int64_t* util;           // nullable: utilization accumulator [E+1]
+  int32_t* seg_acc;        // [E] running totals, zero between calls
+  int* err;                // nullable: device error word (bounds checks of the debug build)
 };
+
+// The last router block: segment starts (exclusive prefix of the totals),
+// counts, tile table and utilization; then the totals go back to zero.  All
+// threads call it; s_warp: 32 ints, s_seg: E+1 ints (shared memory).
+__device__ void finish_from_totals(const FusedScan& scan, int32_t E, int32_t k, int32_t T, int32_t* s_seg) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) {
+    int run = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const int c = e < E ? __ldcg(scan.seg_acc + e) : 0;
+      const int incl = dispatch::warp_inclusive_scan(c);
+      if (e < E) s_seg[e] = run + incl - c;
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+      s_seg[E] = run;
+      (void)in_bounds(run == T * k, scan.err);  // every token has exactly k picks
+    }
+  }
+  __syncthreads();
+  dispatch::finish_segments(E, scan.BM, s_seg, scan.counts, scan.seg_start, scan.mtile_start, scan.util, k);
+  for (int e = threadIdx.x; e < E; e += blockDim.x) scan.seg_acc[e] = 0;
+}
 
 // ------------------------------------------------------------------ F32 router
 
@@ -125,7 +165,6 @@ __global__ void __launch_bounds__(kTopkTPB) topk_from_scores_kernel(const float*
                                                                    const float* __restrict__ scales, int32_t T,
                                                                    int32_t E, int32_t k, RouterOut out,
                                                                    FusedScan scan) {
-  __shared__ int32_t s_warp[32];
   __shared__ int32_t s_seg[257];
   __shared__ int s_last;
   __shared__ int32_t s_sel[kMaxTopK * kTopkTPB];
@@ -183,17 +222,17 @@ __global__ void __launch_bounds__(kTopkTPB) topk_from_scores_kernel(const float*
     for (int r = 0; r < k; ++r) s_sel[r * kTopkTPB + tok] = -1;
   }
   __syncthreads();
-  rank_block_picks(s_sel, k, kTopkTPB, E, T, blk_tok0, s_cnt, s_intra, out.lrank, out.blk_hist + blockIdx.x,
-                   gridDim.x);
-  if (scan.done == nullptr) return;
+  const bool fused = scan.done != nullptr;
+  rank_block_picks(s_sel, k, kTopkTPB, E, T, blk_tok0, s_cnt, s_intra, out.lrank,
+                   (fused ? scan.blk_base : out.blk_hist) + blockIdx.x, gridDim.x, fused ? scan.seg_acc : nullptr);
+  if (!fused) return;
   __syncthreads();
   __threadfence();
   if (threadIdx.x == 0) s_last = atomicAdd(scan.done, 1) == (int)gridDim.x - 1;
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  dispatch::scan_segments_block(out.blk_hist, gridDim.x, E, scan.BM, scan.counts, scan.seg_start, scan.blk_base,
-                                scan.mtile_start, s_warp, s_seg, scan.util, k);
+  finish_from_totals(scan, E, k, T, s_seg);
   if (threadIdx.x == 0) *scan.done = 0;
 }
 

@@ -12,8 +12,9 @@
 //                   applies the sigmoid and keeps its top k on (score, ~index)
 //                   keys in registers -- MoERouter::route (moe.rs:79-107) for
 //                   one token per thread, no shuffles
-// then all 6 warps rank the block's picks and write its histogram
-// (rank_block_picks), and the last block to finish runs the segment scan.
+// then all 6 warps rank the block's picks and claim the block's rows of each
+// expert's segment (rank_block_picks), and the last block to finish turns
+// the per-expert totals into the segment tables (finish_from_totals).
 // x is read from HBM exactly once, by TMA; the gate (E x d BF16) stays in L2.
 #pragma once
 
@@ -70,7 +71,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) route_tc_kernel(
   __shared__ int32_t s_cnt[(SEL / 32) * kMaxExpertsTC];
   __shared__ float s_bias[kMaxExpertsTC];
   __shared__ float s_scale[kMaxExpertsTC];
-  __shared__ int32_t s_warp[32];
   __shared__ int32_t s_seg[kMaxExpertsTC + 1];
   __shared__ int s_last;
 
@@ -169,7 +169,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) route_tc_kernel(
 #pragma unroll
       for (int r = 0; r < kMaxTopK; ++r) best[r] = 0ull;
       tc::tc_fence_after();
-#pragma unroll
+      // Phase 1: the row's sigmoid scores from TMEM into shared memory.  The
+      // stage ring is idle once the accumulator is complete (every MMA, and
+      // so every copy into the ring, has retired); rows are padded by one
+      // float so that a warp's accesses to one expert hit 32 banks.
+      float* s_sc = reinterpret_cast<float*>(smem);
+      const int ld = npad + 1;
+#pragma unroll 1
       for (int c = 0; c < NL; ++c) {
         uint32_t v[32];
         tc::tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
@@ -179,19 +185,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) route_tc_kernel(
           const int e = c * 32 + j;
           if (e < E) {
             const float dot = __fadd_rn(__uint_as_float(v[j]), s_bias[e]);
-            const float sc = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-dot)));
-            unsigned long long kv =
-                ((unsigned long long)__float_as_uint(sc) << 32) | (unsigned long long)(0xFFFFu - (unsigned)e);
-            // keep best[0..k) sorted descending: bubble the new key in
+            s_sc[row * ld + e] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-dot)));
+          }
+        }
+      }
+      // Phase 2: the top k in a compact loop (an unrolled walk over 128
+      // experts would not fit the instruction cache): most keys fail the test
+      // against the current k-th key and cost a compare.
+      unsigned long long kth = 0ull;  // best[k - 1]
+#pragma unroll 1
+      for (int e = 0; e < E; ++e) {
+        unsigned long long kv = ((unsigned long long)__float_as_uint(s_sc[row * ld + e]) << 32) |
+                                (unsigned long long)(0xFFFFu - (unsigned)e);
+        if (kv > kth) {
+          // keep best[0..k) sorted descending: bubble the new key in
 #pragma unroll
-            for (int r = 0; r < kMaxTopK; ++r) {
-              if (r < k && kv > best[r]) {
-                const unsigned long long tmp = best[r];
-                best[r] = kv;
-                kv = tmp;
-              }
+          for (int r = 0; r < kMaxTopK; ++r) {
+            if (r < k && kv > best[r]) {
+              const unsigned long long tmp = best[r];
+              best[r] = kv;
+              kv = tmp;
             }
           }
+#pragma unroll
+          for (int r = 0; r < kMaxTopK; ++r)
+            if (r == k - 1) kth = best[r];
         }
       }
     }
@@ -215,19 +233,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) route_tc_kernel(
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols)
                  : "memory");
   }
-  rank_block_picks(s_sel, k, kTcTPB, E, T, tok0, s_cnt, s_intra, out.lrank, out.blk_hist + blockIdx.x, gridDim.x);
-  if (scan.done == nullptr) return;
+  const bool fused = scan.done != nullptr;
+  rank_block_picks(s_sel, k, kTcTPB, E, T, tok0, s_cnt, s_intra, out.lrank,
+                   (fused ? scan.blk_base : out.blk_hist) + blockIdx.x, gridDim.x, fused ? scan.seg_acc : nullptr);
+  if (!fused) return;
   __syncthreads();
   __threadfence();
   if (threadIdx.x == 0) s_last = atomicAdd(scan.done, 1) == (int)gridDim.x - 1;
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  // the stage ring is free now: stage the histograms there for the scan
-  const int buf_ints = (nstages * stage_bytes) / 4;
-  dispatch::scan_segments_block_staged(out.blk_hist, gridDim.x, E, scan.BM, scan.counts, scan.seg_start,
-                                       scan.blk_base, scan.mtile_start, s_warp, s_seg, scan.util, k,
-                                       reinterpret_cast<int32_t*>(smem), buf_ints);
+  finish_from_totals(scan, E, k, T, s_seg);
   if (threadIdx.x == 0) *scan.done = 0;
 #endif
 }

@@ -91,6 +91,10 @@ struct Params {
   // EPI_COMBINE_BF16: y is token-major (pick (t, i) at row t*k + i) and
   // dst_row is not read.
   int32_t y_token_major;
+  // Rows of the output buffer(s) and of y, for the bounds checks of the debug
+  // build (0: unchecked).
+  int64_t out_rows;
+  int64_t y_rows;
 };
 
 // Output base and row shift of the tile's group.
@@ -305,6 +309,7 @@ __device__ __forceinline__ void write_chunk64_staged(void* C, int64_t ldc, int r
 __device__ __forceinline__ void write_chunk64_staged_mapped(void* C, int64_t ldc, int32_t myrow, int col,
                                                             const uint32_t (&p0)[16], const uint32_t (&p1)[16],
                                                             uint8_t* stage, int lane) {
+  // myrow < 0: not written (a row past the tile's end, or one that failed a bounds check)
   const int sw = lane & 7;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -416,6 +421,10 @@ __device__ __forceinline__ void combine_prepare(const Params& p, int32_t row0, i
     if (valid && i < p.k) {
       dst[i] = p.y_token_major ? row * p.k + i : __ldg(p.dst_row + (int64_t)row * p.k + i);
       wv[i] = __ldg(p.wts + (int64_t)row * p.k + i);
+      if (!in_bounds(p.y_rows == 0 || (dst[i] >= 0 && dst[i] < p.y_rows), p.err)) {
+        dst[i] = 0;
+        wv[i] = 0.f;
+      }
     }
   }
   if (valid) {
@@ -442,6 +451,10 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
   const int orow = row + shift;
   const int wrow0 = row0 + q * 32 + shift;
   const int wrows = max(0, min(32, rows - q * 32));
+  // the tile rows this warp writes (the row-mapped store checks its own rows)
+  const bool rows_ok =
+      in_bounds(p.out_rows == 0 || p.out_rowmap != nullptr || wrows == 0 || (wrow0 >= 0 && wrow0 + wrows <= p.out_rows),
+                lane == 0 ? p.err : nullptr);
   if constexpr (epi_gated(EPI)) {
     constexpr int HALF = BN / 2;
     constexpr int SPAN = HALF / 2;
@@ -453,6 +466,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
       tmem_ld_wait();
       uint32_t pk[16];
       activate_chunk32<EPI>(g, u, pk);
+      if (!rows_ok) continue;
       if (stage) write_chunk32_staged(C, p.ldc, wrow0, wrows, nt * HALF + c, pk, stage, lane);
       else if (valid) write_chunk32_direct(C, p.ldc, orow, nt * HALF + c, pk);
     }
@@ -465,6 +479,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
       tmem_ld_wait();
       uint32_t pk[16];
       combine_chunk32(p, row, nt * BN + c, valid, g, cdst, cwv, pk);
+      if (!rows_ok) continue;
       if (stage) write_chunk32_staged(C, p.ldc, wrow0, wrows, nt * BN + c, pk, stage, lane);
       else if (valid) write_chunk32_direct(C, p.ldc, orow, nt * BN + c, pk);
     }
@@ -472,7 +487,8 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
     constexpr int SPAN = BN / 2;
     if constexpr (EPI == EPI_STORE_BF16) {
       if (stage) {
-        const int32_t myrow = !valid ? -1 : (p.out_rowmap ? __ldg(p.out_rowmap + row) : orow);
+        int32_t myrow = !valid ? -1 : (p.out_rowmap ? __ldg(p.out_rowmap + row) : orow);
+        if (myrow >= 0 && !in_bounds(p.out_rows == 0 || myrow < p.out_rows, p.err)) myrow = -1;
 #pragma unroll 1
         for (int c = part * SPAN; c < (part + 1) * SPAN; c += 64) {
           uint32_t g0[32], g1[32];
@@ -483,7 +499,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
           activate_chunk32<EPI>(g0, g0, pk0);
           activate_chunk32<EPI>(g1, g1, pk1);
           if (p.out_rowmap) write_chunk64_staged_mapped(C, p.ldc, myrow, nt * BN + c, pk0, pk1, stage, lane);
-          else write_chunk64_staged(C, p.ldc, wrow0, wrows, nt * BN + c, pk0, pk1, stage, lane);
+          else if (rows_ok) write_chunk64_staged(C, p.ldc, wrow0, wrows, nt * BN + c, pk0, pk1, stage, lane);
         }
         return;
       }
@@ -496,12 +512,15 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
       tmem_ld32(t_base + c, g);
       tmem_ld_wait();
       if constexpr (EPI == EPI_STORE_F32) {
-        if (valid) store_chunk32<EPI>(C, p.ldc, orow, nt * BN + c, g, g);
+        if (valid && rows_ok) store_chunk32<EPI>(C, p.ldc, orow, nt * BN + c, g, g);
       } else {
         uint32_t pk[16];
         activate_chunk32<EPI>(g, g, pk);
-        if (stage) write_chunk32_staged(C, p.ldc, wrow0, wrows, nt * BN + c, pk, stage, lane);
-        else if (valid) write_chunk32_direct(C, p.ldc, orow_m, nt * BN + c, pk);
+        if (stage) {
+          if (rows_ok) write_chunk32_staged(C, p.ldc, wrow0, wrows, nt * BN + c, pk, stage, lane);
+        } else if (valid && in_bounds(p.out_rows == 0 || (orow_m >= 0 && orow_m < p.out_rows), p.err)) {
+          write_chunk32_direct(C, p.ldc, orow_m, nt * BN + c, pk);
+        }
       }
     }
   }

@@ -33,6 +33,16 @@ def test_library_exports_every_declared_symbol(pkg):
     assert exported == set(header_functions())
 
 
+def test_check_build_exports_the_same_symbols(pkg):
+    """The bounds-checked debug build (build.py --check) is a drop-in for the
+    product library: same exported entry points."""
+    path = os.path.join(PKG_DIR, "libnoor_moe_check.so")
+    assert os.path.exists(path), "build the debug library: python noor_-_bangla_ai_b200/build.py --check"
+    ctypes.CDLL(path)
+    out = subprocess.run(["nm", "-D", "--defined-only", path], capture_output=True, text=True).stdout
+    assert set(re.findall(r"\bT (noor_\w+)", out)) == set(header_functions())
+
+
 def test_library_does_not_link_nccl_or_cuda_driver(pkg):
     out = subprocess.run(["ldd", pkg.api.LIB_PATH], capture_output=True, text=True).stdout
     assert "libnccl" not in out and "libcuda.so" not in out

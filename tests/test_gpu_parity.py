@@ -188,6 +188,24 @@ def test_edge_permutation_and_split(pkg):
     h.close()
 
 
+@pytest.mark.parametrize("name,tokens", [("edge", 6000), ("max_layer", 3000)])
+def test_repeat_calls_bit_identical(pkg, name, tokens):
+    """The router's blocks claim their rows of each expert's segment with
+    atomics, so the row order inside a segment changes from call to call;
+    every row is computed on its own and returns to its token through the row
+    map, so outputs, picks and counts must not change at all."""
+    cfg = pkg.workloads.CONFIGS[name].with_tokens(tokens)
+    w = pkg.workloads.make_weights(cfg)
+    xb = _io(cfg, pkg, pkg.workloads.make_tokens(cfg))
+    h = _handle(pkg, cfg, w, cfg.tokens)
+    first = h.forward_host(xb)
+    for _ in range(3):
+        again = h.forward_host(xb)
+        for a, b in zip(first, again):
+            assert np.array_equal(a, b)
+    h.close()
+
+
 def test_device_mode_matches_host_mode(pkg):
     import torch
     cfg = pkg.workloads.CONFIGS["edge"].with_tokens(3000)
