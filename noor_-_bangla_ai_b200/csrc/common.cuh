@@ -141,6 +141,18 @@ __device__ __forceinline__ float act_silu(float x) { return __fdiv_rn(x, __fadd_
 // for x < -88 gives x / inf = -0, the limit of silu.
 __device__ __forceinline__ float act_silu_bf16out(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
+// GELU (tanh form) for outputs rounded to BF16: 0.5 (1 + tanh u) equals the
+// logistic 1 / (1 + exp(-2u)) exactly, so gelu(x) = x / (1 + exp(-2u)) with
+// u = sqrt(2/pi) (x + 0.044715 x^3) as the reference forms it; the fast
+// exponential and divide stay within a few f32 ulp, far below the BF16
+// rounding that follows (the same bound as act_silu_bf16out).
+__device__ __forceinline__ float act_gelu_tanh_bf16out(float x) {
+  const float sqrt_2_pi = 0x1.988452p-1f;
+  const float cube = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
+  const float inner = __fmul_rn(sqrt_2_pi, __fadd_rn(x, cube));
+  return __fdividef(x, 1.0f + __expf(-2.0f * inner));
+}
+
 __device__ __forceinline__ float act_gelu_tanh(float x) {
   // (2.0f32 / PI).sqrt() evaluated in f32, as the reference does: 0x1.988452p-1
   const float sqrt_2_pi = 0x1.988452p-1f;

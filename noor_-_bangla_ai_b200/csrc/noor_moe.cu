@@ -1559,35 +1559,36 @@ static int launch_norm(noor_moe_handle* h, cudaStream_t s, int kind, const void*
                        const void* resid, int64_t T, void* out) {
   if (T == 0) return NOOR_MOE_OK;
   const unsigned grid = (unsigned)((T + norm::kWarps - 1) / norm::kWarps);
-  const int nv = h->bf16 && h->d % 256 == 0 ? h->d / 256 : 0;  // 16-byte pieces a lane keeps in registers
+  const int smem = norm::staged_smem_bytes(h->bf16, h->d);  // BF16 rows staged in shared memory
+  if (smem > 48 * 1024) {
+    CKR(ensure_smem_limit(norm::rms_norm_rows_kernel<bf16, true, true>, smem));
+    CKR(ensure_smem_limit(norm::rms_norm_rows_kernel<bf16, false, true>, smem));
+  }
   return launch(h, s, kind, [&] {
     if (h->bf16) {
       const bf16* xb = (const bf16*)x;
-      const bf16* rb = (const bf16*)resid;
       bf16* ob = (bf16*)out;
-#define NOOR_NORM_BF16(NV)                                                                                      \
-  if (resid)                                                                                                   \
-    norm::rms_norm_rows_kernel<bf16, true, NV><<<grid, norm::kWarps * 32, 0, s>>>(xb, w, h->norm_eps,          \
-                                                                                  h->depth_scale, rb,          \
-                                                                                  (int32_t)T, h->d, ob);       \
-  else                                                                                                         \
-    norm::rms_norm_rows_kernel<bf16, false, NV><<<grid, norm::kWarps * 32, 0, s>>>(xb, w, h->norm_eps,         \
-                                                                                   h->depth_scale, nullptr,    \
-                                                                                   (int32_t)T, h->d, ob);
-      switch (nv) {
-        case 4: NOOR_NORM_BF16(4) break;
-        case 8: NOOR_NORM_BF16(8) break;
-        case 12: NOOR_NORM_BF16(12) break;
-        case 16: NOOR_NORM_BF16(16) break;
-        default: NOOR_NORM_BF16(0) break;
+      if (smem > 0) {
+        if (resid)
+          norm::rms_norm_rows_kernel<bf16, true, true><<<grid, norm::kWarps * 32, smem, s>>>(
+              xb, w, h->norm_eps, h->depth_scale, (const bf16*)resid, (int32_t)T, h->d, ob);
+        else
+          norm::rms_norm_rows_kernel<bf16, false, true><<<grid, norm::kWarps * 32, smem, s>>>(
+              xb, w, h->norm_eps, h->depth_scale, nullptr, (int32_t)T, h->d, ob);
+      } else {
+        if (resid)
+          norm::rms_norm_rows_kernel<bf16, true, false><<<grid, norm::kWarps * 32, 0, s>>>(
+              xb, w, h->norm_eps, h->depth_scale, (const bf16*)resid, (int32_t)T, h->d, ob);
+        else
+          norm::rms_norm_rows_kernel<bf16, false, false><<<grid, norm::kWarps * 32, 0, s>>>(
+              xb, w, h->norm_eps, h->depth_scale, nullptr, (int32_t)T, h->d, ob);
       }
-#undef NOOR_NORM_BF16
     } else {
       if (resid)
-        norm::rms_norm_rows_kernel<float, true, 0><<<grid, norm::kWarps * 32, 0, s>>>(
+        norm::rms_norm_rows_kernel<float, true, false><<<grid, norm::kWarps * 32, 0, s>>>(
             (const float*)x, w, h->norm_eps, h->depth_scale, (const float*)resid, (int32_t)T, h->d, (float*)out);
       else
-        norm::rms_norm_rows_kernel<float, false, 0><<<grid, norm::kWarps * 32, 0, s>>>(
+        norm::rms_norm_rows_kernel<float, false, false><<<grid, norm::kWarps * 32, 0, s>>>(
             (const float*)x, w, h->norm_eps, h->depth_scale, nullptr, (int32_t)T, h->d, (float*)out);
     }
   });

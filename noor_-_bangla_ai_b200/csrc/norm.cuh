@@ -20,6 +20,10 @@ namespace noor {
 namespace norm {
 
 constexpr int kWarps = 8;
+// At least 3 blocks (24 warps) per SM: the kernel is latency-bound per warp
+// (a serial f64 sum, then the square root), so it needs warps in flight more
+// than registers; this caps it at 85 registers a thread.
+constexpr int kMinBlocks = 3;
 
 template <typename T_>
 struct Row8;
@@ -67,48 +71,55 @@ __device__ __forceinline__ float norm_one(float x, double rms, double r, float w
 
 // out[t] = (resid[t] +) f32(f64(x[t]) / rms * f64(w)) * depth_scale, rms =
 // sqrt(sum_i x_i^2 / d + eps) in f64 (x_i^2 is exact in f64, so a fused
-// multiply-add equals the reference's multiply then add).
-// NV > 0 (BF16 rows, d = 256 * NV): each lane keeps its NV 16-byte pieces of
-// the row in registers, so the row is read from memory once.  NV == 0: any d
-// that is a multiple of 8, the row read twice (the second time from L1/L2).
-// Rows 16-byte aligned.
-template <typename T_, bool RESID, int NV>
-__global__ void __launch_bounds__(kWarps * 32) rms_norm_rows_kernel(const T_* __restrict__ x,
-                                                                    const float* __restrict__ w, double eps,
-                                                                    float depth_scale, const T_* __restrict__ resid,
-                                                                    int32_t T, int32_t d, T_* __restrict__ out) {
+// multiply-add equals the reference's multiply then add).  d a multiple of 8,
+// rows 16-byte aligned.
+// STAGE (BF16 rows): each warp keeps its row in shared memory (dynamic,
+// kWarps * d * 2 bytes), so the row is read from memory once and each
+// thread's state stays small; without it the row is read twice (the second
+// time from L1/L2).  Either way lane l sums elements 8l + 256j .. +7 in that
+// order.
+template <typename T_, bool RESID, bool STAGE>
+__global__ void __launch_bounds__(kWarps * 32, kMinBlocks) rms_norm_rows_kernel(const T_* __restrict__ x,
+                                                                                const float* __restrict__ w,
+                                                                                double eps, float depth_scale,
+                                                                                const T_* __restrict__ resid,
+                                                                                int32_t T, int32_t d,
+                                                                                T_* __restrict__ out) {
+  extern __shared__ uint4 s_rows[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int32_t t = blockIdx.x * kWarps + warp;
   if (t >= T) return;
   const T_* row = x + (int64_t)t * d;
   double ss = 0.0;
-  if constexpr (NV > 0) {
-    static_assert(sizeof(T_) == 2, "register-resident rows are BF16");
-    uint4 v[NV];
-    const uint4* rv = reinterpret_cast<const uint4*>(row);
-#pragma unroll
-    for (int i = 0; i < NV; ++i) v[i] = __ldg(rv + lane + 32 * i);
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const uint32_t u[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+  if constexpr (STAGE) {
+    static_assert(sizeof(T_) == 2, "staged rows are BF16");
+    const int nvec = d >> 3;  // 16-byte pieces of the row
+    uint4* srow = s_rows + (int64_t)warp * nvec;
+    const uint4* gx = reinterpret_cast<const uint4*>(row);
+#pragma unroll 4
+    for (int i = lane; i < nvec; i += 32) {
+      const uint4 v = __ldg(gx + i);
+      srow[i] = v;
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const double a = (double)bf16_lo(u[j]), b = (double)bf16_hi(u[j]);
+        const double a = (double)bf16_lo(u[j]), bb = (double)bf16_hi(u[j]);
         ss = __fma_rn(a, a, ss);
-        ss = __fma_rn(b, b, ss);
+        ss = __fma_rn(bb, bb, ss);
       }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
     const double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)d), eps));
     const double r = __drcp_rn(rms);
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int c = (lane + 32 * i) * 8;
+#pragma unroll 2
+    for (int i = lane; i < nvec; i += 32) {
+      const int c = i * 8;
+      const uint4 v = srow[i];
       const float4 wa = __ldg(reinterpret_cast<const float4*>(w + c));
       const float4 wb = __ldg(reinterpret_cast<const float4*>(w + c + 4));
       const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-      const uint32_t u[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
       float o[8];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -151,6 +162,12 @@ __global__ void __launch_bounds__(kWarps * 32) rms_norm_rows_kernel(const T_* __
       Row8<T_>::store(out + (int64_t)t * d + c, o);
     }
   }
+}
+
+// Shared memory of the staged BF16 form (0 when rows are read twice).
+inline int staged_smem_bytes(bool bf16, int d) {
+  const int bytes = kWarps * d * 2;
+  return bf16 && bytes <= 64 * 1024 ? bytes : 0;
 }
 
 }  // namespace norm

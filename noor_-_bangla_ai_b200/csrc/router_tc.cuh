@@ -169,6 +169,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) route_tc_kernel(
 #pragma unroll
       for (int r = 0; r < kMaxTopK; ++r) best[r] = 0ull;
       tc::tc_fence_after();
+      if constexpr (NL == 1) {
+        // up to 32 experts: one TMEM load, and the insertion of every key
+        // unrolled (fits the instruction cache, no dependent loop)
+        uint32_t v[32];
+        tc::tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16), v);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          if (e < E) {
+            const float dot = __fadd_rn(__uint_as_float(v[e]), s_bias[e]);
+            const float sc = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-dot)));
+            unsigned long long kv =
+                ((unsigned long long)__float_as_uint(sc) << 32) | (unsigned long long)(0xFFFFu - (unsigned)e);
+#pragma unroll
+            for (int r = 0; r < kMaxTopK; ++r) {
+              if (r < k && kv > best[r]) {
+                const unsigned long long tmp = best[r];
+                best[r] = kv;
+                kv = tmp;
+              }
+            }
+          }
+        }
+      } else {
       // Phase 1: the row's sigmoid scores from TMEM into shared memory.  The
       // stage ring is idle once the accumulator is complete (every MMA, and
       // so every copy into the ring, has retired); rows are padded by one
@@ -211,6 +235,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) route_tc_kernel(
           for (int r = 0; r < kMaxTopK; ++r)
             if (r == k - 1) kth = best[r];
         }
+      }
       }
     }
 #pragma unroll

@@ -33,7 +33,14 @@ namespace tc {
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one 128B swizzle row
 constexpr int STAGES = 4;
-constexpr int EPI_WARPS = 8;  // two warps per TMEM lane quarter, each on half the columns
+#ifndef NOOR_GEMM_EPI_WARPS
+#define NOOR_GEMM_EPI_WARPS 8
+#endif
+// Epilogue warps: EPI_PARTS per TMEM lane quarter, each on 1/EPI_PARTS of the
+// tile's columns.
+constexpr int EPI_WARPS = NOOR_GEMM_EPI_WARPS;
+constexpr int EPI_PARTS = EPI_WARPS / 4;
+static_assert(EPI_WARPS % 4 == 0 && (EPI_PARTS == 1 || EPI_PARTS == 2 || EPI_PARTS == 4), "epilogue warps");
 constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
 
 enum Epilogue : int {
@@ -236,8 +243,8 @@ __device__ __forceinline__ void activate_chunk32(const uint32_t (&v)[32], const 
       a = __fmul_rn(act_silu_bf16out(a), __uint_as_float(u[2 * j]));
       b = __fmul_rn(act_silu_bf16out(b), __uint_as_float(u[2 * j + 1]));
     } else if constexpr (EPI == EPI_GEGLU_BF16) {
-      a = __fmul_rn(act_gelu_tanh(a), __uint_as_float(u[2 * j]));
-      b = __fmul_rn(act_gelu_tanh(b), __uint_as_float(u[2 * j + 1]));
+      a = __fmul_rn(act_gelu_tanh_bf16out(a), __uint_as_float(u[2 * j]));
+      b = __fmul_rn(act_gelu_tanh_bf16out(b), __uint_as_float(u[2 * j + 1]));
     }
     p[j] = pack_bf16(a, b);
   }
@@ -410,7 +417,7 @@ __device__ __forceinline__ void combine_chunk32(const Params& p, int row, int co
 template <int BN>
 __device__ __forceinline__ void combine_prepare(const Params& p, int32_t row0, int32_t rows, int32_t nt, int q,
                                                 int part, int lane, int32_t (&dst)[8], float (&wv)[8]) {
-  constexpr int SPAN = BN / 2;
+  constexpr int SPAN = BN / EPI_PARTS;
   const int row_in_tile = q * 32 + lane;
   const bool valid = row_in_tile < rows;
   const int row = row0 + row_in_tile;
@@ -457,7 +464,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
                 lane == 0 ? p.err : nullptr);
   if constexpr (epi_gated(EPI)) {
     constexpr int HALF = BN / 2;
-    constexpr int SPAN = HALF / 2;
+    constexpr int SPAN = HALF / EPI_PARTS;
 #pragma unroll 1
     for (int c = part * SPAN; c < (part + 1) * SPAN; c += 32) {
       uint32_t g[32], u[32];
@@ -471,7 +478,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
       else if (valid) write_chunk32_direct(C, p.ldc, orow, nt * HALF + c, pk);
     }
   } else if constexpr (EPI == EPI_COMBINE_BF16) {
-    constexpr int SPAN = BN / 2;
+    constexpr int SPAN = BN / EPI_PARTS;
 #pragma unroll 1
     for (int c = part * SPAN; c < (part + 1) * SPAN; c += 32) {
       uint32_t g[32];
@@ -484,7 +491,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
       else if (valid) write_chunk32_direct(C, p.ldc, orow, nt * BN + c, pk);
     }
   } else {
-    constexpr int SPAN = BN / 2;
+    constexpr int SPAN = BN / EPI_PARTS;
     if constexpr (EPI == EPI_STORE_BF16) {
       if (stage) {
         int32_t myrow = !valid ? -1 : (p.out_rowmap ? __ldg(p.out_rowmap + row) : orow);
@@ -662,7 +669,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ---------------- epilogue: warp w owns TMEM lanes 32*(w%4) .. +31 and
     // one half of the tile's columns
     const int q = warp & 3;
-    const int part = (warp - 2) >> 2;  // 0: first half of the columns, 1: second
+    const int part = (warp - 2) >> 2;  // which 1/EPI_PARTS of the columns
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int32_t tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
@@ -960,7 +967,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ---------------- epilogue (both CTAs): this CTA's 128 rows of the pair tile
     const int q = warp & 3;
-    const int part = (warp - 2) >> 2;
+    const int part = (warp - 2) >> 2;  // which 1/EPI_PARTS of the columns
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int32_t tile = cid; tile < total_tiles; tile += nclusters) {
