@@ -134,6 +134,22 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// The same test with a suspend-time hint: the thread sleeps in the wait until
+// the phase completes or about 20 us pass, instead of taking issue slots from
+// the producer and MMA threads while it polls.  Used by the epilogue warps,
+// which wait a whole tile's mainloop for each accumulator.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(20000u)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -154,7 +170,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (code == DEV_TIMEOUT_EPILOGUE ? mbar_try_wait_sleep(bar, parity) : mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
     if (clock64() - start > kWaitLimitCycles) {
       *abort_flag = 1;
