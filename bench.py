@@ -150,6 +150,38 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# ------------------------------------------------------------------ host NUMA placement
+
+def bind_to_gpu_numa(torch, local_rank):
+    """Run this process on the host CPUs attached to its GPU's PCIe root, so
+    that the pinned host buffers of the e2e measurement are first touched --
+    and placed -- on the GPU's own NUMA node.  Returns what was done (for the
+    JSON line); leaves the affinity alone when the topology is not visible."""
+    try:
+        p = torch.cuda.get_device_properties(local_rank)
+        addr = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        base = os.path.join("/sys/bus/pci/devices", addr)
+        with open(os.path.join(base, "local_cpulist")) as f:
+            spec = f.read().strip()
+        cpus = set()
+        for part in spec.split(","):
+            a, _, b = part.partition("-")
+            cpus.update(range(int(a), int(b or a) + 1))
+        cpus &= os.sched_getaffinity(0)
+        node = -1
+        try:
+            with open(os.path.join(base, "numa_node")) as f:
+                node = int(f.read().strip())
+        except OSError:
+            pass
+        if not cpus:
+            return {"pci": addr, "bound": False}
+        os.sched_setaffinity(0, cpus)
+        return {"pci": addr, "numa_node": node, "cpus": len(cpus), "bound": True}
+    except Exception as e:  # no sysfs view of the device
+        return {"bound": False, "why": type(e).__name__}
+
+
 # ------------------------------------------------------------------ CPU baseline
 
 CPU_MOE_SAMPLE = {"proxy_tiny": 2048, "edge": 2048, "edge_skewed": 2048, "pro": 256, "max_layer": 128}
@@ -547,6 +579,10 @@ def run_ours(args):
     rank, local_rank, world = env_rank()
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    # the e2e copies want each rank's pinned buffers on its GPU's NUMA node;
+    # the CPU baseline gets every host core back before it starts its threads
+    all_cpus = os.sched_getaffinity(0)
+    numa = bind_to_gpu_numa(torch, local_rank)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     ctx = Ctx(torch, dist, rank, local_rank, world, dev)
@@ -607,9 +643,11 @@ def run_ours(args):
         }
         if "ep_parity" in r:
             line["ep_parity"] = r["ep_parity"]
+        line["host_numa"] = numa
         if pro is not None:
             line["pro"] = pro
         if world == 1 and not args.no_cpu_baseline and not args.sublayer:
+            os.sched_setaffinity(0, all_cpus)
             v, cores, dt, n, blas = cpu_baseline(cfg, r["weights"], r["x"])
             line["cpu_baseline"] = {
                 "value": v, "unit": UNIT, "cores": cores, "kind": "port",
