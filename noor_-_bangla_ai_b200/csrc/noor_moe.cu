@@ -243,6 +243,9 @@ struct noor_moe_handle {
   int64_t tm_user_T = -1;
 
   cudaStream_t own = nullptr, aux = nullptr;
+  int gemm_pair_cap = 0;  // SM pairs the SM-pair GEMMs may take (0: all); set while a kernel shares the GPU
+  int dispatch_sms = 0;   // peer exchange: SMs the permute runs on beside the dense up projection (0: in line)
+  bool dispatch_bulk = false;  // peer exchange: permute with bulk copies instead of thread loads/stores
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_done = nullptr;
   int* d_err = nullptr;
 
@@ -621,7 +624,8 @@ int launch_tc2(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& 
   }
   set_peer_out(p, po);
   const int64_t tiles = std::max<int64_t>(1, max_tiles * p.n_tiles);
-  const int clusters = (int)std::min<int64_t>(h->num_sms / 2, tiles);
+  const int pairs = h->gemm_pair_cap > 0 ? std::min(h->gemm_pair_cap, h->num_sms / 2) : h->num_sms / 2;
+  const int clusters = (int)std::min<int64_t>(pairs, tiles);
   return launch(h, s, kind, [&] { kern<<<2 * clusters, tc::NUM_THREADS, tc::Cfg2<EPI>::SMEM_BYTES, s>>>(tA, tB, p); });
 }
 
@@ -875,6 +879,16 @@ constexpr bool kForkSidePeer = false;
 // the same as the single in-line permute (24.2-24.4M tokens/s either way),
 // so it is off.
 constexpr bool kSplitPermutePeer = false;
+// Under the peer-memory exchange with a dense branch, the permute (NVLink
+// stores) can run on a second stream on dispatch_sms SMs while the dense up
+// projection, which needs only x, runs on the others.  Each permute block
+// asks for kDispatchSmem of shared memory (the bulk permute's row ring; the
+// thread permute leaves it unused) so that it cannot share an SM with a GEMM
+// CTA: two blocks fill one SM, and the GEMM is launched with the remaining SM
+// pairs.  (Spreading both kernels over every SM was slower.)  Set per
+// process: NOOR_MOE_DISPATCH_SMS (default 0: the permute runs in line on
+// every SM) and NOOR_MOE_DISPATCH=bulk|threads (default threads).
+constexpr int kDispatchSmem = 96 * 1024;
 
 // Wait, bounded, for the setup collectives queued on the handle's stream.
 int setup_sync(noor_moe_handle* h) {
@@ -1013,6 +1027,10 @@ int peer_setup(noor_moe_handle* h) {
   P::Peers peers{};
   peers.G = G;
   peers.me = me;
+  const char* senv = std::getenv("NOOR_MOE_DISPATCH_SMS");
+  h->dispatch_sms = senv ? std::max(0, std::min(std::atoi(senv), h->num_sms / 2)) & ~1 : 0;
+  const char* denv = std::getenv("NOOR_MOE_DISPATCH");
+  h->dispatch_bulk = denv && std::strcmp(denv, "bulk") == 0 && (d * 2) % 16 == 0;
   const char* tenv = std::getenv("NOOR_MOE_PEER_TIMEOUT_MS");
   const int64_t tms = tenv ? std::max<int64_t>(1, std::atoll(tenv)) : 10000;
   peers.timeout_ns = tms * 1000000LL;
@@ -1125,7 +1143,22 @@ int run_forward_peer(noor_moe_handle* h, cudaStream_t s, const void* x, const CU
     CKR(side_branches());
     CK(cudaEventRecord(h->ev_join, h->aux));
   }
+  const int row_bytes = d * 2;
+  const int bulk_slots = std::min(P::kBulkSlotsMax, kDispatchSmem / row_bytes);
+  // the bulk permute on `blocks` one-warp blocks with kDispatchSmem of ring each
+  auto permute_bulk = [&](cudaStream_t st, unsigned blocks) -> int {
+    return launch(h, st, K_PERMUTE, [&] {
+      P::permute_peer_bulk_kernel<<<blocks, 32, kDispatchSmem, st>>>(
+          static_cast<const uint8_t*>(x), row_bytes, (int32_t)T, k, (int32_t)((T + tpb - 1) / tpb), tpb,
+          h->idx.as<int32_t>(), h->lrank.as<int32_t>(), h->blk_base.as<int32_t>(), h->seg_start.as<int32_t>(),
+          h->dest_base.as<int32_t>(), h->El, h->peers, h->pstatus.as<int>(), h->dst_row.as<int32_t>(), cap_rows,
+          bulk_slots, h->d_err);
+    });
+  };
+  const bool bulk = h->dispatch_bulk && bulk_slots >= 2;
+  if (bulk) CKR(ensure_smem_limit(P::permute_peer_bulk_kernel, kDispatchSmem));
   auto permute = [&](cudaStream_t st, int part, bool persistent) -> int {
+    if (bulk && part == P::PERMUTE_ALL) return permute_bulk(st, (unsigned)(2 * h->num_sms));
     return launch(h, st, K_PERMUTE, [&] {
       const int64_t blocks = (T + P::kPermuteWarps - 1) / P::kPermuteWarps;
       const unsigned grid = (unsigned)(persistent ? std::min<int64_t>(blocks, h->num_sms) : blocks);
@@ -1137,7 +1170,31 @@ int run_forward_peer(noor_moe_handle* h, cudaStream_t s, const void* x, const CU
     });
   };
   const bool split = kSplitPermutePeer && !fork && T > 0;
-  if (split) {
+  const bool overlap = h->dispatch_sms > 0 && !fork && !split && T > 0 && side;
+  if (overlap) {
+    // the dispatch on its own SMs (second stream), the dense/shared up
+    // projections on the rest; joined before the barrier
+    CK(cudaEventRecord(h->ev_fork, s));
+    CK(cudaStreamWaitEvent(h->aux, h->ev_fork, 0));
+    if (bulk) {
+      CKR(permute_bulk(h->aux, (unsigned)(2 * h->dispatch_sms)));
+    } else {
+      CKR(ensure_smem_limit(P::permute_peer_kernel, kDispatchSmem));
+      CKR(launch(h, h->aux, K_PERMUTE, [&] {
+        P::permute_peer_kernel<<<2 * h->dispatch_sms, P::kPermuteWarps * 32, kDispatchSmem, h->aux>>>(
+            static_cast<const uint8_t*>(x), row_bytes, (int32_t)T, k, (int32_t)((T + tpb - 1) / tpb), tpb,
+            h->idx.as<int32_t>(), h->lrank.as<int32_t>(), h->blk_base.as<int32_t>(), h->seg_start.as<int32_t>(),
+            h->dest_base.as<int32_t>(), h->El, h->peers, h->pstatus.as<int>(), h->dst_row.as<int32_t>(),
+            P::PERMUTE_ALL, cap_rows, h->d_err);
+      }));
+    }
+    CK(cudaEventRecord(h->ev_join, h->aux));
+    h->gemm_pair_cap = (h->num_sms - h->dispatch_sms) / 2;
+    const int rc = side_branches();
+    h->gemm_pair_cap = 0;
+    CKR(rc);
+    CK(cudaStreamWaitEvent(s, h->ev_join, 0));
+  } else if (split) {
     // remote rows on the second stream (persistent grid: it shares the SMs
     // with the GEMM beside it); local rows and the dense branch in line
     CK(cudaEventRecord(h->ev_fork, s));
@@ -1148,7 +1205,7 @@ int run_forward_peer(noor_moe_handle* h, cudaStream_t s, const void* x, const CU
   } else if (T > 0) {
     CKR(permute(s, P::PERMUTE_ALL, fork));
   }
-  if (side && !fork) CKR(side_branches());  // in line, while the other ranks' rows arrive
+  if (side && !fork && !overlap) CKR(side_branches());  // in line, while the other ranks' rows arrive
   if (split) CK(cudaStreamWaitEvent(s, h->ev_join, 0));
   auto barrier = [&]() -> int {
     return launch(h, s, K_EP_BARRIER, [&] {

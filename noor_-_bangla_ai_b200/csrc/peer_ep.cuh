@@ -343,5 +343,173 @@ __global__ void __launch_bounds__(kPermuteWarps * 32) permute_peer_kernel(
   __threadfence_system();  // the rows are visible on their owners before the next barrier signals
 }
 
+// ---- the dispatch with bulk copies (TMA engine) instead of thread loads and
+// stores: one warp per block; lane 0 moves whole rows through a ring of row
+// slots in shared memory -- one bulk load per token, one bulk store per pick
+// straight into the owner's receive buffer -- while lanes 0..k-1 compute the
+// picks' rows and write the row maps.  Because the copy engine moves the
+// bytes, a few SMs keep NVLink busy, and the kernel can run on SMs that a GEMM
+// leaves free (it asks for the ring's shared memory, which keeps GEMM CTAs
+// off its SMs).  Same results as permute_peer_kernel (PERMUTE_ALL).
+
+__device__ __forceinline__ uint32_t bulk_smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Global -> shared, completing `bytes` on the barrier.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   bulk_smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(bulk_smem_addr(bar))
+               : "memory");
+}
+
+// Shared -> global (this GPU's memory or a peer's), tracked by bulk groups.
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(bulk_smem_addr(src)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Every bulk group but the newest n (0 <= n <= 16) has finished reading
+// shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read_c() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_read(int n) {
+  switch (n) {
+    case 0: bulk_wait_read_c<0>(); break;
+    case 1: bulk_wait_read_c<1>(); break;
+    case 2: bulk_wait_read_c<2>(); break;
+    case 3: bulk_wait_read_c<3>(); break;
+    case 4: bulk_wait_read_c<4>(); break;
+    case 5: bulk_wait_read_c<5>(); break;
+    case 6: bulk_wait_read_c<6>(); break;
+    case 7: bulk_wait_read_c<7>(); break;
+    case 8: bulk_wait_read_c<8>(); break;
+    case 9: bulk_wait_read_c<9>(); break;
+    case 10: bulk_wait_read_c<10>(); break;
+    case 11: bulk_wait_read_c<11>(); break;
+    case 12: bulk_wait_read_c<12>(); break;
+    case 13: bulk_wait_read_c<13>(); break;
+    case 14: bulk_wait_read_c<14>(); break;
+    case 15: bulk_wait_read_c<15>(); break;
+    default: bulk_wait_read_c<16>(); break;
+  }
+}
+
+// Every bulk group has completed (its writes are performed).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+constexpr int kBulkSlotsMax = 32;
+
+__global__ void __launch_bounds__(32) permute_peer_bulk_kernel(
+    const uint8_t* __restrict__ x, int32_t row_bytes, int32_t T, int32_t k, int32_t nblk, int32_t tpb,
+    const int32_t* __restrict__ idx, const int32_t* __restrict__ lrank, const int32_t* __restrict__ blk_base,
+    const int32_t* __restrict__ seg_start, const int32_t* __restrict__ dest_base, int32_t El, Peers P,
+    const int* __restrict__ status, int32_t* __restrict__ dst_row, int64_t cap_rows, int32_t nslots, int* err) {
+  extern __shared__ __align__(128) uint8_t ring[];  // nslots rows
+  __shared__ __align__(8) uint64_t full[kBulkSlotsMax];
+  const int lane = threadIdx.x;
+  const bool store = *status == STATUS_OK;
+  const int32_t first = blockIdx.x;
+  const int32_t n = first < T ? (T - 1 - first) / (int32_t)gridDim.x + 1 : 0;  // tokens of this block
+  if (lane == 0) {
+    for (int i = 0; i < nslots; ++i)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bulk_smem_addr(&full[i])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  const int pending = nslots / 2 < 16 ? (nslots / 2 > 1 ? nslots / 2 : 1) : 16;  // store groups in flight
+  int32_t issued = 0;  // tokens whose load lane 0 has issued
+  auto load = [&](int32_t j) {  // token j of this block into slot j % nslots (lane 0)
+    issued = j + 1;
+    const int slot = j % nslots;
+    const int32_t t = first + j * (int32_t)gridDim.x;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bulk_smem_addr(&full[slot])),
+                 "r"((uint32_t)row_bytes)
+                 : "memory");
+    bulk_load(ring + (int64_t)slot * row_bytes, x + (int64_t)t * row_bytes, (uint32_t)row_bytes, &full[slot]);
+  };
+  // lane 0: wait, bounded, until token j's row is in its slot
+  auto wait_row = [&](int32_t j) -> bool {
+    const uint32_t bar = bulk_smem_addr(&full[j % nslots]);
+    const uint32_t parity = (uint32_t)((j / nslots) & 1);
+    const uint64_t t0 = global_ns();
+    uint32_t done = 0;
+    while (!done) {
+      asm volatile(
+          "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+          : "=r"(done)
+          : "r"(bar), "r"(parity)
+          : "memory");
+      if (!done && (int64_t)(global_ns() - t0) > P.timeout_ns) break;
+    }
+    return done != 0;
+  };
+  if (lane == 0 && store)
+    for (int32_t j = 0; j < n && j < nslots; ++j) load(j);
+  bool ok = true;
+  int32_t waited = 0;  // tokens whose row lane 0 has seen arrive
+  for (int32_t j = 0; j < n; ++j) {
+    const int32_t t = first + j * (int32_t)gridDim.x;
+    // lane i < k: pick i of token t -- its row here (dst_row), and where it
+    // goes on the expert's owner (the owner's row map records t*k + i)
+    uint8_t* dst = nullptr;
+    if (lane < k) {
+      const int32_t e = __ldg(idx + (int64_t)t * k + lane);
+      const int32_t in_seg = __ldg(blk_base + (int64_t)e * nblk + t / tpb) + __ldg(lrank + (int64_t)t * k + lane);
+      dst_row[(int64_t)t * k + lane] = __ldg(seg_start + e) + in_seg;
+      const int32_t r = e / El;
+      const int32_t remote = __ldg(dest_base + e) + in_seg;
+      if (store && in_bounds(r >= 0 && r < P.G && remote >= 0 && remote < cap_rows, err)) {
+        dst = P.xrecv[r] + (int64_t)remote * row_bytes;
+        P.rowmap[r][remote] = t * k + lane;
+      }
+    }
+    if (!store || !ok) continue;
+    if (lane == 0) {
+      if (wait_row(j)) {
+        waited = j + 1;
+      } else {
+        atomicCAS(err, 0, DEV_TIMEOUT_PRODUCER);
+        ok = false;
+      }
+    }
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    if (!ok) continue;
+    // lane 0 stores the row once per pick, reading each pick's target from its lane
+    for (int i = 0; i < k; ++i) {
+      uint8_t* d = reinterpret_cast<uint8_t*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(dst), i));
+      if (lane == 0 && d != nullptr) bulk_store(d, ring + (int64_t)(j % nslots) * row_bytes, (uint32_t)row_bytes);
+    }
+    if (lane == 0) {
+      bulk_commit();
+      // half the ring holds rows whose stores are in flight, the other half
+      // rows being loaded: the slot of token f = j - pending + 1 is free once
+      // its stores have read it (at most pending - 1 newer groups still
+      // reading); it takes token f + nslots
+      const int32_t f = j - pending + 1;
+      if (f >= 0 && f + nslots < n) {
+        bulk_wait_read(pending - 1);
+        load(f + nslots);
+      }
+    }
+    __syncwarp();
+  }
+  if (lane == 0) {
+    // after a wait gave up, let the loads still in flight land (bounded)
+    // before the block's shared memory is released
+    for (int32_t j = waited; j < issued; ++j) (void)wait_row(j);
+    bulk_wait_all();
+    asm volatile("fence.proxy.async.global;" ::: "memory");  // the copies' writes before generic-proxy signals
+  }
+  __syncwarp();
+  __threadfence_system();  // the rows are visible on their owners before the next barrier signals
+}
+
 }  // namespace peer
 }  // namespace noor

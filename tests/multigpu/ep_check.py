@@ -38,7 +38,15 @@ def main():
     ap.add_argument("--peer-timeout", action="store_true",
                     help="failure detection: rank 0 runs a forward that the other ranks leave out; its bounded "
                          "device wait (1 s) must end with NOOR_MOE_ERR_TIMEOUT and close the exchange")
+    ap.add_argument("--dispatch", choices=("threads", "bulk"), default=None,
+                    help="peer exchange: permute rows with thread loads/stores or with bulk copies")
+    ap.add_argument("--dispatch-sms", type=int, default=None,
+                    help="peer exchange: run the permute on this many SMs beside the dense up projection")
     args = ap.parse_args()
+    if args.dispatch:
+        os.environ["NOOR_MOE_DISPATCH"] = args.dispatch
+    if args.dispatch_sms is not None:
+        os.environ["NOOR_MOE_DISPATCH_SMS"] = str(args.dispatch_sms)
     if args.transport == "nccl":
         os.environ["NOOR_MOE_EP_TRANSPORT"] = "nccl"
     if args.peer_timeout:

@@ -29,11 +29,16 @@ def _run(n, *extra):
     ("--transport", "peer", "--uneven"),            # one rank with no tokens, the others ragged
     ("--transport", "peer", "--overflow"),          # an over-capacity batch is refused on every rank, then exact
     ("--transport", "peer", "--peer-timeout"),      # a rank that never joins: bounded wait, TIMEOUT, exchange closed
+    ("--transport", "peer", "--dispatch", "bulk", "--graph"),                        # bulk-copy permute in line
+    ("--transport", "peer", "--dispatch", "bulk", "--dispatch-sms", "16", "--uneven"),  # ... beside the dense GEMM
+    ("--transport", "peer", "--dispatch", "threads", "--dispatch-sms", "16"),          # thread permute beside it
     ("--transport", "nccl"),                        # the NCCL all-to-all-v exchange
     ("--transport", "nccl", "--uneven"),
     ("--config", "proxy_tiny", "--tokens", "777"),  # F32 layer (NCCL exchange)
     ("--config", "pro", "--tokens", "4000", "--transport", "peer"),        # E = 64, k = 6 over 2/4/8 owners
     ("--config", "max_layer", "--tokens", "2000", "--transport", "peer"),  # E = 128, k = 8
+    ("--config", "max_layer", "--tokens", "2000", "--transport", "peer", "--dispatch", "bulk",
+     "--dispatch-sms", "16"),
 ])
 def test_expert_parallel_matches_single_gpu(extra):
     n = min(_ngpu(), 8)
