@@ -881,14 +881,16 @@ constexpr bool kForkSidePeer = false;
 constexpr bool kSplitPermutePeer = false;
 // Under the peer-memory exchange with a dense branch, the permute (NVLink
 // stores) can run on a second stream on dispatch_sms SMs while the dense up
-// projection, which needs only x, runs on the others.  Each permute block
-// asks for kDispatchSmem of shared memory (the bulk permute's row ring; the
-// thread permute leaves it unused) so that it cannot share an SM with a GEMM
-// CTA: two blocks fill one SM, and the GEMM is launched with the remaining SM
-// pairs.  (Spreading both kernels over every SM was slower.)  Set per
-// process: NOOR_MOE_DISPATCH_SMS (default 0: the permute runs in line on
-// every SM) and NOOR_MOE_DISPATCH=bulk|threads (default threads).
+// projection, which needs only x, runs on the others.  The permute's blocks
+// ask for enough shared memory that no GEMM CTA fits beside them (the bulk
+// permute: two one-warp blocks per SM, each with a kDispatchSmem row ring;
+// the thread permute: one 16-warp block per SM with kDispatchSmemSide,
+// unused), and the GEMM is launched with the remaining SM pairs.  (Spreading
+// both kernels over every SM was slower.)  Set per process:
+// NOOR_MOE_DISPATCH_SMS (default 0: the permute runs in line on every SM)
+// and NOOR_MOE_DISPATCH=bulk|threads (default threads).
 constexpr int kDispatchSmem = 96 * 1024;
+constexpr int kDispatchSmemSide = 160 * 1024;
 
 // Wait, bounded, for the setup collectives queued on the handle's stream.
 int setup_sync(noor_moe_handle* h) {
@@ -1162,7 +1164,7 @@ int run_forward_peer(noor_moe_handle* h, cudaStream_t s, const void* x, const CU
     return launch(h, st, K_PERMUTE, [&] {
       const int64_t blocks = (T + P::kPermuteWarps - 1) / P::kPermuteWarps;
       const unsigned grid = (unsigned)(persistent ? std::min<int64_t>(blocks, h->num_sms) : blocks);
-      P::permute_peer_kernel<<<grid, P::kPermuteWarps * 32, 0, st>>>(
+      P::permute_peer_kernel<P::kPermuteWarps><<<grid, P::kPermuteWarps * 32, 0, st>>>(
           static_cast<const uint8_t*>(x), d * 2, (int32_t)T, k, (int32_t)((T + tpb - 1) / tpb), tpb,
           h->idx.as<int32_t>(), h->lrank.as<int32_t>(), h->blk_base.as<int32_t>(), h->seg_start.as<int32_t>(),
           h->dest_base.as<int32_t>(), h->El, h->peers, h->pstatus.as<int>(), h->dst_row.as<int32_t>(), part,
@@ -1179,9 +1181,11 @@ int run_forward_peer(noor_moe_handle* h, cudaStream_t s, const void* x, const CU
     if (bulk) {
       CKR(permute_bulk(h->aux, (unsigned)(2 * h->dispatch_sms)));
     } else {
-      CKR(ensure_smem_limit(P::permute_peer_kernel, kDispatchSmem));
+      // one 16-warp block per SM; kDispatchSmemSide keeps GEMM CTAs off those SMs
+      CKR(ensure_smem_limit(P::permute_peer_kernel<P::kPermuteWarpsSide>, kDispatchSmemSide));
       CKR(launch(h, h->aux, K_PERMUTE, [&] {
-        P::permute_peer_kernel<<<2 * h->dispatch_sms, P::kPermuteWarps * 32, kDispatchSmem, h->aux>>>(
+        P::permute_peer_kernel<P::kPermuteWarpsSide>
+            <<<h->dispatch_sms, P::kPermuteWarpsSide * 32, kDispatchSmemSide, h->aux>>>(
             static_cast<const uint8_t*>(x), row_bytes, (int32_t)T, k, (int32_t)((T + tpb - 1) / tpb), tpb,
             h->idx.as<int32_t>(), h->lrank.as<int32_t>(), h->blk_base.as<int32_t>(), h->seg_start.as<int32_t>(),
             h->dest_base.as<int32_t>(), h->El, h->peers, h->pstatus.as<int>(), h->dst_row.as<int32_t>(),

@@ -286,10 +286,12 @@ __global__ void __launch_bounds__(32) barrier_kernel(Peers P, uint64_t* seq, int
 // PERMUTE_LOCAL (rows whose expert lives on this rank, plus every dst_row)
 // and PERMUTE_REMOTE (rows bound for other ranks, over NVLink), which can run
 // on different streams.
-constexpr int kPermuteWarps = 4;
+constexpr int kPermuteWarps = 4;       // in line: 4-warp blocks over the whole GPU
+constexpr int kPermuteWarpsSide = 16;  // beside a GEMM: one 16-warp block per SM it is given
 enum PermutePart : int { PERMUTE_ALL = 0, PERMUTE_LOCAL = 1, PERMUTE_REMOTE = 2 };
 
-__global__ void __launch_bounds__(kPermuteWarps * 32) permute_peer_kernel(
+template <int W>
+__global__ void __launch_bounds__(W * 32) permute_peer_kernel(
     const uint8_t* __restrict__ x, int32_t row_bytes, int32_t T, int32_t k, int32_t nblk, int32_t tpb,
     const int32_t* __restrict__ idx, const int32_t* __restrict__ lrank, const int32_t* __restrict__ blk_base,
     const int32_t* __restrict__ seg_start, const int32_t* __restrict__ dest_base, int32_t El, Peers P,
@@ -298,7 +300,7 @@ __global__ void __launch_bounds__(kPermuteWarps * 32) permute_peer_kernel(
   const bool store = *status == STATUS_OK;
   const int nvec = row_bytes >> 4;
   constexpr int U = 8;
-  for (int32_t t = blockIdx.x * kPermuteWarps + warp; t < T; t += gridDim.x * kPermuteWarps) {
+  for (int32_t t = blockIdx.x * W + warp; t < T; t += gridDim.x * W) {
     uint8_t* dst[8];
     const int32_t* bb = blk_base + t / tpb;  // blk_base[e][block] is bb[e * nblk]
     bool any = false;

@@ -370,47 +370,65 @@ __device__ __forceinline__ void store_chunk32(void* C, int64_t ldc, int row, int
   }
 }
 
-// One 32-column chunk of the fused combine for token row `row`, packed to
-// BF16 pairs: moe = sum_i w_i * y_i in rank order from zero, each multiply and
-// add rounded separately (moe.rs:159-165); (+ shared, moe.rs:168-173);
-// out = (dense + moe) * (1/sqrt 2) (parallel_ffn.rs:32-35).
-__device__ __forceinline__ void combine_chunk32(const Params& p, int row, int col, bool valid,
-                                                const uint32_t (&acc)[32], const int32_t (&dst)[8],
-                                                const float (&wv)[8], uint32_t (&o)[16]) {
-  float moe[32];
+// The expert part of one 32-column chunk of the fused combine for token row
+// `row`: moe = sum_i w_i * y_i in rank order from zero, each multiply and add
+// rounded separately (moe.rs:159-165), then + shared (moe.rs:168-173).  Runs
+// before the chunk's accumulator is read, so only these registers are live
+// while the gathers are in flight.
+__device__ __forceinline__ void combine_moe32(const Params& p, int row, int col, bool valid, const int32_t (&dst)[8],
+                                              const float (&wv)[8], float (&moe)[32]) {
 #pragma unroll
   for (int j = 0; j < 32; ++j) moe[j] = 0.f;
-  if (valid) {
+  if (!valid) return;
+  // picks in pairs: both picks' loads are issued before either is used, so a
+  // chunk waits for memory once per pair (batches of 4 spill at the 168
+  // registers that 10 warps leave a thread, and measured slower)
+  constexpr int KB = 2;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (i < p.k) {
-        const uint4* yp = reinterpret_cast<const uint4*>(p.y + (int64_t)dst[i] * p.ldc + col);
-        uint4 yv[4];
+  for (int i0 = 0; i0 < 8; i0 += KB) {
+    if (i0 < p.k) {
+      uint4 yv[KB][4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) yv[q] = __ldg(yp + q);
+      for (int b = 0; b < KB; ++b) {
+        if (i0 + b < p.k) {
+          const uint4* yp = reinterpret_cast<const uint4*>(p.y + (int64_t)dst[i0 + b] * p.ldc + col);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint32_t u[4] = {yv[q].x, yv[q].y, yv[q].z, yv[q].w};
+          for (int q = 0; q < 4; ++q) yv[b][q] = __ldg(yp + q);
+        }
+      }
 #pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            moe[8 * q + 2 * r] = __fadd_rn(moe[8 * q + 2 * r], __fmul_rn(wv[i], bf16_lo(u[r])));
-            moe[8 * q + 2 * r + 1] = __fadd_rn(moe[8 * q + 2 * r + 1], __fmul_rn(wv[i], bf16_hi(u[r])));
+      for (int b = 0; b < KB; ++b) {
+        if (i0 + b < p.k) {
+          const float wi = wv[i0 + b];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t u[4] = {yv[b][q].x, yv[b][q].y, yv[b][q].z, yv[b][q].w};
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              moe[8 * q + 2 * r] = __fadd_rn(moe[8 * q + 2 * r], __fmul_rn(wi, bf16_lo(u[r])));
+              moe[8 * q + 2 * r + 1] = __fadd_rn(moe[8 * q + 2 * r + 1], __fmul_rn(wi, bf16_hi(u[r])));
+            }
           }
         }
       }
     }
-    if (p.shared) {
-      const float4* sp = reinterpret_cast<const float4*>(p.shared + (int64_t)row * p.ldc + col);
+  }
+  if (p.shared) {
+    const float4* sp = reinterpret_cast<const float4*>(p.shared + (int64_t)row * p.ldc + col);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float4 v = __ldg(sp + q);
-        moe[4 * q] = __fadd_rn(moe[4 * q], v.x);
-        moe[4 * q + 1] = __fadd_rn(moe[4 * q + 1], v.y);
-        moe[4 * q + 2] = __fadd_rn(moe[4 * q + 2], v.z);
-        moe[4 * q + 3] = __fadd_rn(moe[4 * q + 3], v.w);
-      }
+    for (int q = 0; q < 8; ++q) {
+      const float4 v = __ldg(sp + q);
+      moe[4 * q] = __fadd_rn(moe[4 * q], v.x);
+      moe[4 * q + 1] = __fadd_rn(moe[4 * q + 1], v.y);
+      moe[4 * q + 2] = __fadd_rn(moe[4 * q + 2], v.z);
+      moe[4 * q + 3] = __fadd_rn(moe[4 * q + 3], v.w);
     }
   }
+}
+
+// out = (dense + moe) * (1/sqrt 2) as BF16 pairs (parallel_ffn.rs:32-35).
+__device__ __forceinline__ void combine_finish32(const uint32_t (&acc)[32], const float (&moe)[32],
+                                                 uint32_t (&o)[16]) {
   const float inv_sqrt2 = 0x1.6a09e6p-1f;  // 1.0f32 / 2.0f32.sqrt()
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
@@ -497,11 +515,13 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
     constexpr int SPAN = BN / EPI_PARTS;
 #pragma unroll 1
     for (int c = part * SPAN; c < (part + 1) * SPAN; c += 32) {
+      float moe[32];
+      combine_moe32(p, row, nt * BN + c, valid, cdst, cwv, moe);
       uint32_t g[32];
       tmem_ld32(t_base + c, g);
       tmem_ld_wait();
       uint32_t pk[16];
-      combine_chunk32(p, row, nt * BN + c, valid, g, cdst, cwv, pk);
+      combine_finish32(g, moe, pk);
       if (!rows_ok) continue;
       if (stage) write_chunk32_staged(C, p.ldc, wrow0, wrows, nt * BN + c, pk, stage, lane);
       else if (valid) write_chunk32_direct(C, p.ldc, orow, nt * BN + c, pk);
