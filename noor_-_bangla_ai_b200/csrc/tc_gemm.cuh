@@ -370,6 +370,15 @@ __device__ __forceinline__ void store_chunk32(void* C, int64_t ldc, int row, int
   }
 }
 
+// One 32-byte read-only load (a 256-bit vector load: half the instructions,
+// and so half the L1 wavefronts, of 16-byte loads when the lanes' addresses
+// fall in different rows).  p must be 32-byte aligned.
+__device__ __forceinline__ void ldg256(const void* p, uint32_t (&r)[8]) {
+  asm volatile("ld.global.nc.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "l"(p));
+}
+
 // The expert part of one 32-column chunk of the fused combine for token row
 // `row`: moe = sum_i w_i * y_i in rank order from zero, each multiply and add
 // rounded separately (moe.rs:159-165), then + shared (moe.rs:168-173).  Runs
@@ -387,13 +396,13 @@ __device__ __forceinline__ void combine_moe32(const Params& p, int row, int col,
 #pragma unroll
   for (int i0 = 0; i0 < 8; i0 += KB) {
     if (i0 < p.k) {
-      uint4 yv[KB][4];
+      uint32_t yv[KB][16];
 #pragma unroll
       for (int b = 0; b < KB; ++b) {
         if (i0 + b < p.k) {
-          const uint4* yp = reinterpret_cast<const uint4*>(p.y + (int64_t)dst[i0 + b] * p.ldc + col);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) yv[b][q] = __ldg(yp + q);
+          const bf16* yp = p.y + (int64_t)dst[i0 + b] * p.ldc + col;
+          ldg256(yp, *reinterpret_cast<uint32_t(*)[8]>(&yv[b][0]));
+          ldg256(yp + 16, *reinterpret_cast<uint32_t(*)[8]>(&yv[b][8]));
         }
       }
 #pragma unroll
@@ -401,27 +410,22 @@ __device__ __forceinline__ void combine_moe32(const Params& p, int row, int col,
         if (i0 + b < p.k) {
           const float wi = wv[i0 + b];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t u[4] = {yv[b][q].x, yv[b][q].y, yv[b][q].z, yv[b][q].w};
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-              moe[8 * q + 2 * r] = __fadd_rn(moe[8 * q + 2 * r], __fmul_rn(wi, bf16_lo(u[r])));
-              moe[8 * q + 2 * r + 1] = __fadd_rn(moe[8 * q + 2 * r + 1], __fmul_rn(wi, bf16_hi(u[r])));
-            }
+          for (int r = 0; r < 16; ++r) {
+            moe[2 * r] = __fadd_rn(moe[2 * r], __fmul_rn(wi, bf16_lo(yv[b][r])));
+            moe[2 * r + 1] = __fadd_rn(moe[2 * r + 1], __fmul_rn(wi, bf16_hi(yv[b][r])));
           }
         }
       }
     }
   }
   if (p.shared) {
-    const float4* sp = reinterpret_cast<const float4*>(p.shared + (int64_t)row * p.ldc + col);
+    const float* sp = p.shared + (int64_t)row * p.ldc + col;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 v = __ldg(sp + q);
-      moe[4 * q] = __fadd_rn(moe[4 * q], v.x);
-      moe[4 * q + 1] = __fadd_rn(moe[4 * q + 1], v.y);
-      moe[4 * q + 2] = __fadd_rn(moe[4 * q + 2], v.z);
-      moe[4 * q + 3] = __fadd_rn(moe[4 * q + 3], v.w);
+    for (int q = 0; q < 4; ++q) {
+      uint32_t v[8];
+      ldg256(sp + 8 * q, v);
+#pragma unroll
+      for (int r = 0; r < 8; ++r) moe[8 * q + r] = __fadd_rn(moe[8 * q + r], __uint_as_float(v[r]));
     }
   }
 }
