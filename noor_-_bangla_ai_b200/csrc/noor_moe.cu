@@ -244,7 +244,8 @@ struct noor_moe_handle {
 
   cudaStream_t own = nullptr, aux = nullptr;
   int gemm_pair_cap = 0;  // SM pairs the SM-pair GEMMs may take (0: all); set while a kernel shares the GPU
-  int dispatch_sms = 0;   // peer exchange: SMs the permute runs on beside the dense up projection (0: in line)
+  int dispatch_sms = 0;   // peer exchange: SMs the permute runs on beside the dense up projection (0: in line),
+                          // set by peer_setup
   bool dispatch_bulk = false;  // peer exchange: permute with bulk copies instead of thread loads/stores
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_done = nullptr;
   int* d_err = nullptr;
@@ -626,7 +627,8 @@ int launch_tc2(noor_moe_handle* h, cudaStream_t s, int kind, const CUtensorMap& 
   const int64_t tiles = std::max<int64_t>(1, max_tiles * p.n_tiles);
   const int pairs = h->gemm_pair_cap > 0 ? std::min(h->gemm_pair_cap, h->num_sms / 2) : h->num_sms / 2;
   const int clusters = (int)std::min<int64_t>(pairs, tiles);
-  return launch(h, s, kind, [&] { kern<<<2 * clusters, tc::NUM_THREADS, tc::Cfg2<EPI>::SMEM_BYTES, s>>>(tA, tB, p); });
+  return launch(h, s, kind,
+                [&] { kern<<<2 * clusters, tc::Cfg2<EPI>::THREADS, tc::Cfg2<EPI>::SMEM_BYTES, s>>>(tA, tB, p); });
 }
 
 // A tensor-core GEMM with the layer's tile shape: SM pairs with 256-row
@@ -886,9 +888,12 @@ constexpr bool kSplitPermutePeer = false;
 // permute: two one-warp blocks per SM, each with a kDispatchSmem row ring;
 // the thread permute: one 16-warp block per SM with kDispatchSmemSide,
 // unused), and the GEMM is launched with the remaining SM pairs.  (Spreading
-// both kernels over every SM was slower.)  Set per process:
-// NOOR_MOE_DISPATCH_SMS (default 0: the permute runs in line on every SM)
-// and NOOR_MOE_DISPATCH=bulk|threads (default threads).
+// both kernels over every SM was slower.)  On two B200s, Edge-like layer:
+// in line 1.301 ms/step; 24 / 32 / 48 SMs beside the GEMM 1.238 / 1.187 /
+// 1.209 ms.  Set per process: NOOR_MOE_DISPATCH_SMS (default
+// kDispatchSMsDefault; 0 runs the permute in line on every SM) and
+// NOOR_MOE_DISPATCH=bulk|threads (default threads).
+constexpr int kDispatchSMsDefault = 32;
 constexpr int kDispatchSmem = 96 * 1024;
 constexpr int kDispatchSmemSide = 160 * 1024;
 
@@ -1030,7 +1035,7 @@ int peer_setup(noor_moe_handle* h) {
   peers.G = G;
   peers.me = me;
   const char* senv = std::getenv("NOOR_MOE_DISPATCH_SMS");
-  h->dispatch_sms = senv ? std::max(0, std::min(std::atoi(senv), h->num_sms / 2)) & ~1 : 0;
+  h->dispatch_sms = std::max(0, std::min(senv ? std::atoi(senv) : kDispatchSMsDefault, h->num_sms / 2)) & ~1;
   const char* denv = std::getenv("NOOR_MOE_DISPATCH");
   h->dispatch_bulk = denv && std::strcmp(denv, "bulk") == 0 && (d * 2) % 16 == 0;
   const char* tenv = std::getenv("NOOR_MOE_PEER_TIMEOUT_MS");

@@ -42,6 +42,13 @@ constexpr int EPI_WARPS = NOOR_GEMM_EPI_WARPS;
 constexpr int EPI_PARTS = EPI_WARPS / 4;
 static_assert(EPI_WARPS % 4 == 0 && (EPI_PARTS == 1 || EPI_PARTS == 2 || EPI_PARTS == 4), "epilogue warps");
 constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
+// The SM-pair kernel sets its epilogue warp count per epilogue: the plain
+// and gated epilogues (one TMEM read and a store per chunk) with
+// NOOR_GEMM_EPI_WARPS_PLAIN warps, the fused combine (gathers that need
+// warps in flight) with EPI_WARPS.
+#ifndef NOOR_GEMM_EPI_WARPS_PLAIN
+#define NOOR_GEMM_EPI_WARPS_PLAIN 8
+#endif
 
 enum Epilogue : int {
   EPI_STORE_BF16 = 0,   // C = acc (bf16)
@@ -452,10 +459,10 @@ __device__ __forceinline__ void combine_finish32(const uint32_t (&acc)[32], cons
 // column range of those rows.  The epilogue calls it before it waits for the
 // tile's accumulator, so the gathers of y overlap the tile's MMAs and the
 // chunk loop finds them in L2.
-template <int BN>
+template <int BN, int PARTS = EPI_PARTS>
 __device__ __forceinline__ void combine_prepare(const Params& p, int32_t row0, int32_t rows, int32_t nt, int q,
                                                 int part, int lane, int32_t (&dst)[8], float (&wv)[8]) {
-  constexpr int SPAN = BN / EPI_PARTS;
+  constexpr int SPAN = BN / PARTS;
   const int row_in_tile = q * 32 + lane;
   const bool valid = row_in_tile < rows;
   const int row = row0 + row_in_tile;
@@ -486,7 +493,7 @@ __device__ __forceinline__ void combine_prepare(const Params& p, int32_t row0, i
 
 // Outputs go to rows + shift of C (the combine reads its inputs at the
 // unshifted rows).  cdst / cwv: the combine's inputs from combine_prepare.
-template <int BN, int EPI>
+template <int BN, int EPI, int PARTS = EPI_PARTS>
 __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t shift, uint32_t t_base, int32_t row0,
                                               int32_t rows, int32_t nt, int q, int part, int lane, uint8_t* stage,
                                               const int32_t (&cdst)[8], const float (&cwv)[8]) {
@@ -502,7 +509,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
                 lane == 0 ? p.err : nullptr);
   if constexpr (epi_gated(EPI)) {
     constexpr int HALF = BN / 2;
-    constexpr int SPAN = HALF / EPI_PARTS;
+    constexpr int SPAN = HALF / PARTS;
 #pragma unroll 1
     for (int c = part * SPAN; c < (part + 1) * SPAN; c += 32) {
       uint32_t g[32], u[32];
@@ -516,7 +523,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
       else if (valid) write_chunk32_direct(C, p.ldc, orow, nt * HALF + c, pk);
     }
   } else if constexpr (EPI == EPI_COMBINE_BF16) {
-    constexpr int SPAN = BN / EPI_PARTS;
+    constexpr int SPAN = BN / PARTS;
 #pragma unroll 1
     for (int c = part * SPAN; c < (part + 1) * SPAN; c += 32) {
       float moe[32];
@@ -531,7 +538,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, void* C, int32_t 
       else if (valid) write_chunk32_direct(C, p.ldc, orow, nt * BN + c, pk);
     }
   } else {
-    constexpr int SPAN = BN / EPI_PARTS;
+    constexpr int SPAN = BN / PARTS;
     if constexpr (EPI == EPI_STORE_BF16) {
       if (stage) {
         int32_t myrow = !valid ? -1 : (p.out_rowmap ? __ldg(p.out_rowmap + row) : orow);
@@ -775,6 +782,10 @@ constexpr int kStaticSmemMargin = 4096;  // group table, barriers
 
 template <int EPI>
 struct Cfg2 {
+  static constexpr int WARPS = EPI == EPI_COMBINE_BF16 ? EPI_WARPS : NOOR_GEMM_EPI_WARPS_PLAIN;  // epilogue warps
+  static constexpr int PARTS = WARPS / 4;
+  static_assert(WARPS % 4 == 0 && (PARTS == 1 || PARTS == 2 || PARTS == 4), "epilogue warps");
+  static constexpr int THREADS = 64 + 32 * WARPS;
   static constexpr int A_BYTES = 128 * BK * 2;  // this CTA's A half
   static constexpr int B_BYTES = 128 * BK * 2;  // this CTA's B half
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -783,10 +794,10 @@ struct Cfg2 {
   // combine's gathers)
   static constexpr int STAGE_OUT_BYTES = EPI == EPI_STORE_BF16 ? 4096 : 2048;
   // the requested depth, or as many stages as fit beside the output staging
-  static constexpr int FIT = (kSmemLimit - kStaticSmemMargin - EPI_WARPS * STAGE_OUT_BYTES - 1024) / STAGE_BYTES;
+  static constexpr int FIT = (kSmemLimit - kStaticSmemMargin - WARPS * STAGE_OUT_BYTES - 1024) / STAGE_BYTES;
   static constexpr int STAGES = NOOR_GEMM_STAGES < FIT ? NOOR_GEMM_STAGES : FIT;
   static_assert(STAGES >= 2 && STAGES <= kMaxStages2, "operand ring depth");
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_WARPS * STAGE_OUT_BYTES + 1024;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + WARPS * STAGE_OUT_BYTES + 1024;
   static constexpr uint32_t TMEM_COLS = 512;  // two 256-column accumulators
   static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
                                     ((uint32_t)(256 >> 4) << 24);
@@ -850,7 +861,7 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint64_t* bar, uint32_t rank
 }
 
 template <int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg2<EPI>::THREADS, 1)
     grouped_gemm_2cta_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                              const Params p) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
@@ -861,7 +872,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smA = smem;
   uint8_t* smB = smem + STAGES2 * C::A_BYTES;
-  uint8_t* smOut = smem + STAGES2 * C::STAGE_BYTES;  // EPI_WARPS x STAGE_OUT_BYTES
+  uint8_t* smOut = smem + STAGES2 * C::STAGE_BYTES;  // C::WARPS x STAGE_OUT_BYTES
 
   __shared__ __align__(8) uint64_t full_bar[kMaxStages2];
   __shared__ __align__(8) uint64_t empty_bar[kMaxStages2];
@@ -883,7 +894,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&accf_bar[a], 1);
-      mbar_init(&acce_bar[a], 2 * EPI_WARPS);  // epilogue warps of both CTAs (leader's copy is used)
+      mbar_init(&acce_bar[a], 2 * C::WARPS);  // epilogue warps of both CTAs (leader's copy is used)
     }
     mbar_init(&drain_bar, 1);
     abort_flag = 0;
@@ -1007,7 +1018,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ---------------- epilogue (both CTAs): this CTA's 128 rows of the pair tile
     const int q = warp & 3;
-    const int part = (warp - 2) >> 2;  // which 1/EPI_PARTS of the columns
+    const int part = (warp - 2) >> 2;  // which 1/C::PARTS of the columns
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int32_t tile = cid; tile < total_tiles; tile += nclusters) {
@@ -1015,15 +1026,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const int32_t row0 = tc.row0 + 128 * (int32_t)rank, rows = tc.rows - 128 * (int32_t)rank;
       int32_t cdst[8];
       float cwv[8];
-      if constexpr (EPI == EPI_COMBINE_BF16) combine_prepare<BN>(p, row0, rows, tc.nt, q, part, lane, cdst, cwv);
+      if constexpr (EPI == EPI_COMBINE_BF16) combine_prepare<BN, C::PARTS>(p, row0, rows, tc.nt, q, part, lane, cdst, cwv);
       if (!mbar_wait(&accf_bar[acc], acc_phase, &abort_flag, p.err, DEV_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t t_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       void* Ct;
       int32_t shift;
       tile_output(p, tc.g, &Ct, &shift);
-      epilogue_tile<BN, EPI>(p, Ct, shift, t_base, row0, rows, tc.nt, q, part, lane,
-                             smOut + (warp - 2) * C::STAGE_OUT_BYTES, cdst, cwv);
+      epilogue_tile<BN, EPI, C::PARTS>(p, Ct, shift, t_base, row0, rows, tc.nt, q, part, lane,
+                                       smOut + (warp - 2) * C::STAGE_OUT_BYTES, cdst, cwv);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {

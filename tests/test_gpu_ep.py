@@ -25,13 +25,14 @@ def _run(n, *extra):
 
 
 @pytest.mark.parametrize("extra", [
-    ("--transport", "peer", "--graph"),             # BF16: NVLink peer-memory exchange, eager + CUDA graph
+    ("--transport", "peer", "--graph"),             # BF16: NVLink peer-memory exchange (permute on 32 SMs
+                                                    # beside the dense GEMM), eager + CUDA graph
     ("--transport", "peer", "--uneven"),            # one rank with no tokens, the others ragged
     ("--transport", "peer", "--overflow"),          # an over-capacity batch is refused on every rank, then exact
     ("--transport", "peer", "--peer-timeout"),      # a rank that never joins: bounded wait, TIMEOUT, exchange closed
-    ("--transport", "peer", "--dispatch", "bulk", "--graph"),                        # bulk-copy permute in line
+    ("--transport", "peer", "--dispatch", "bulk", "--dispatch-sms", "0", "--graph"),  # bulk-copy permute in line
     ("--transport", "peer", "--dispatch", "bulk", "--dispatch-sms", "16", "--uneven"),  # ... beside the dense GEMM
-    ("--transport", "peer", "--dispatch", "threads", "--dispatch-sms", "16"),          # thread permute beside it
+    ("--transport", "peer", "--dispatch", "threads", "--dispatch-sms", "0"),           # thread permute in line
     ("--transport", "nccl"),                        # the NCCL all-to-all-v exchange
     ("--transport", "nccl", "--uneven"),
     ("--config", "proxy_tiny", "--tokens", "777"),  # F32 layer (NCCL exchange)
