@@ -738,7 +738,7 @@ int launch_route_tc(noor_moe_handle* h, cudaStream_t s, const CUtensorMap& tmx, 
   const int npad = router::tc_npad(E);
   const int smem = router::tc_smem_bytes(npad);
   // the epilogue stages the tile's scores in the stage ring
-  if (router::tc_stages(npad) * router::tc_stage_bytes(npad) < router::kTcTPB * (npad + 1) * 4)
+  if (npad > 32 && smem - 1024 < router::tc_scores_bytes(npad))
     return fail(NOOR_MOE_ERR_UNSUPPORTED, "router stage ring too small for %d experts", E);
   const unsigned grid = (unsigned)((T + router::kTcTPB - 1) / router::kTcTPB);
   auto go = [&](auto kern) -> int {

@@ -27,7 +27,9 @@ namespace router {
 
 constexpr int kTcTPB = 128;       // tokens per CTA
 constexpr int kTcMaxStages = 8;
-constexpr int kTcRingBytes = 192 * 1024;  // stage ring budget: one CTA per SM
+constexpr int kTcRingBytes = 192 * 1024;     // stage ring budget, E <= 32: one CTA per SM
+constexpr int kTcRingBytesWide = 72 * 1024;  // E > 32: two CTAs per SM, so that one streams x while the
+                                             // other runs its (longer) epilogue
 constexpr int kTcThreads = 192;   // producer, MMA, 4 epilogue warps
 constexpr int kTcXBytes = kTcTPB * 64 * 2;  // one k-block of the x tile
 
@@ -36,10 +38,19 @@ __host__ __device__ constexpr int tc_stage_bytes(int npad) { return kTcXBytes + 
 // As many stages as fit the ring budget, at most kTcMaxStages: each CTA
 // streams 512 KB of x per 128 tokens (d = 2048), and the ring depth is what
 // keeps its TMA -> MMA -> release chain from being latency-bound.
+__host__ __device__ constexpr int tc_ring_budget(int npad) { return npad <= 32 ? kTcRingBytes : kTcRingBytesWide; }
 __host__ __device__ constexpr int tc_stages(int npad) {
-  return kTcRingBytes / tc_stage_bytes(npad) < kTcMaxStages ? kTcRingBytes / tc_stage_bytes(npad) : kTcMaxStages;
+  return tc_ring_budget(npad) / tc_stage_bytes(npad) < kTcMaxStages ? tc_ring_budget(npad) / tc_stage_bytes(npad)
+                                                                     : kTcMaxStages;
 }
-__host__ constexpr int tc_smem_bytes(int npad) { return tc_stages(npad) * tc_stage_bytes(npad) + 1024; }
+// For E > 32 the epilogue stages the tile's scores (kTcTPB rows of npad + 1
+// floats) in the ring once every copy into it has retired.
+__host__ __device__ constexpr int tc_scores_bytes(int npad) { return kTcTPB * (npad + 1) * 4; }
+__host__ constexpr int tc_smem_bytes(int npad) {
+  return (tc_stages(npad) * tc_stage_bytes(npad) > tc_scores_bytes(npad) ? tc_stages(npad) * tc_stage_bytes(npad)
+                                                                         : tc_scores_bytes(npad)) +
+         1024;
+}
 __host__ __device__ constexpr uint32_t tc_tmem_cols(int npad) {
   return npad <= 32 ? 32u : (npad <= 64 ? 64u : 128u);
 }
