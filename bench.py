@@ -28,8 +28,8 @@ per-launch events on an uncaptured pass; tensor-core fractions divide by the
 burst cuBLAS peak (the kernels run inside a ~1 ms step at full clock), with a
 per-GHz figure beside them.
 
-After the headline layer the same run times the Pro-like layer (BASELINE
-config 4, strong scaling over the N GPUs) into the `pro` key, unless
+After the headline layer the same run times the Pro-like layer (131072
+tokens, d=3072, E=64, k=6; strong scaling over the N GPUs) into the `pro` key, unless
 --no-pro or the headline is Pro-like itself.  Under expert parallelism every
 rank then checks its output bit for bit against a single-GPU handle holding
 all experts (`ep_parity`).
