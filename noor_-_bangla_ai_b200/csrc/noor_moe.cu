@@ -1201,8 +1201,8 @@ int run_forward_peer(noor_moe_handle* h, cudaStream_t s, const void* x, const CU
     h->gemm_pair_cap = (h->num_sms - h->dispatch_sms) / 2;
     const int rc = side_branches();
     h->gemm_pair_cap = 0;
+    CK(cudaStreamWaitEvent(s, h->ev_join, 0));  // joined on the error path too (a capture must not end forked)
     CKR(rc);
-    CK(cudaStreamWaitEvent(s, h->ev_join, 0));
   } else if (split) {
     // remote rows on the second stream (persistent grid: it shares the SMs
     // with the GEMM beside it); local rows and the dense branch in line
